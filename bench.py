@@ -1,0 +1,530 @@
+"""Benchmark of the SAE hot path (encode -> CSR -> decode) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2]
+
+One step = one forward pass (fused encode with row counts -> dense_to_csr -> sparse
+decode) over one batch of synthetic tokens. Default workload: BASELINE config 2,
+JumpReLU SAE d_in=2304 d_sae=65536 bf16, 16384 tokens per GPU, inputs generated with
+that config's distributions (seeded; the reference benchmarks on synthetic data too).
+
+Multi-GPU (torchrun, one process per GPU, NCCL): token-sharded with replicated weights,
+per-GPU work fixed ("weak" scaling), no collective on the data path; the timed region
+is bracketed by a barrier + synchronize and the max over ranks is reported.
+
+--impl reference times the reference's own CPU implementation of the path (the CPU
+restatement in oracle/: dense torch SAE encode -> to_sparse_csr -> CSR addmm, as the
+reference's bench does) on the host cores, on a bounded token sample per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "tokens/s encode->CSR->decode"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+CONFIGS = {
+    1: dict(name="cfg1 ReLU fp32 d_in=768 d_sae=16384", activation="relu", d_in=768, d_sae=16384,
+            dtype=torch.float32, tokens=4096),
+    2: dict(name="cfg2 JumpReLU bf16 d_in=2304 d_sae=65536", activation="jumprelu", d_in=2304, d_sae=65536,
+            dtype=torch.bfloat16, tokens=16384, l0=64.0),
+    3: dict(name="cfg3 sparse decode bf16 d_in=2304 d_sae=65536", activation="decode", d_in=2304, d_sae=65536,
+            dtype=torch.bfloat16, tokens=65536, l0=64.0),
+    4: dict(name="cfg4 TopK k=32 bf16 d_in=4096 d_sae=131072", activation="topk", d_in=4096, d_sae=131072,
+            dtype=torch.bfloat16, tokens=32768, k=32),
+}
+
+
+# ------------------------------------------------------------------------------ inputs
+
+def unit_rows(d_sae, d_in, gen, device):
+    W = torch.randn(d_sae, d_in, generator=gen, device=device)
+    W /= W.norm(dim=1, keepdim=True)
+    return W
+
+
+def zipf_probs(d_sae, total, gen, device, s=0.8, cap=0.5):
+    """p_i proportional to rank^-s over a random permutation, scaled to sum `total`, each
+    clipped to <= cap, iterated to a fixpoint (BASELINE config 2 threshold scheme)."""
+    ranks = torch.randperm(d_sae, generator=gen, device=device).double() + 1.0
+    w = ranks.pow(-s)
+    p = w * (total / w.sum())
+    for _ in range(100):
+        p = torch.clamp(p, max=cap)
+        free = p < cap
+        deficit = total - p.sum()
+        if deficit.abs() < 1e-9 or not free.any():
+            break
+        p[free] *= 1.0 + deficit / p[free].sum()
+    return p.clamp(max=cap)
+
+
+def normal_isf(p):
+    """Phi^-1(1 - p) via erfinv (the inverse standard-normal survival function)."""
+    return math.sqrt(2.0) * torch.erfinv(1.0 - 2.0 * p)
+
+
+def make_sae(cfg_id, device, seed=0):
+    """Weights of a config (identical on every rank: same seed)."""
+    from saeflow_b200 import SAE
+
+    c = CONFIGS[cfg_id]
+    gen = torch.Generator(device=device).manual_seed(seed)
+    act = "relu" if c["activation"] == "decode" else c["activation"]
+    sae = SAE.__new__(SAE)
+    torch.nn.Module.__init__(sae)
+    sae.d_in, sae.d_sae, sae.activation, sae.k = c["d_in"], c["d_sae"], act, c.get("k")
+    W_dec = unit_rows(c["d_sae"], c["d_in"], gen, device)
+    dt = c["dtype"]
+    sae.W_dec = torch.nn.Parameter(W_dec.to(dt), requires_grad=False)
+    sae.W_enc = torch.nn.Parameter(W_dec.T.contiguous().to(dt), requires_grad=False)
+    del W_dec
+    sae.b_enc = torch.nn.Parameter(torch.zeros(c["d_sae"], device=device, dtype=dt), requires_grad=False)
+    sae.b_dec = torch.nn.Parameter(torch.zeros(c["d_in"], device=device, dtype=dt), requires_grad=False)
+    sae.threshold = None
+    if cfg_id == 1:
+        sae.b_enc.fill_(-2.66)
+    elif cfg_id in (2, 3):
+        sae.b_dec.copy_((torch.randn(c["d_in"], generator=gen, device=device) * 0.1).to(dt))
+    elif cfg_id == 4:
+        sae.b_enc.copy_((torch.randn(c["d_sae"], generator=gen, device=device) * 0.01).to(dt))
+    if act == "jumprelu":
+        p = zipf_probs(c["d_sae"], c["l0"], gen, device)
+        sae.threshold = torch.nn.Parameter(normal_isf(p).float().to(dt), requires_grad=False)
+    return sae
+
+
+def make_tokens(cfg_id, chunk, device, tokens=None):
+    """Token batch `chunk` of a config (seed + chunk id, so a chunk is the same at any GPU count)."""
+    c = CONFIGS[cfg_id]
+    gen = torch.Generator(device=device).manual_seed(1_000_003 + chunk)
+    T = tokens or c["tokens"]
+    return torch.randn(T, c["d_in"], generator=gen, device=device).to(c["dtype"])
+
+
+def make_csr(cfg_id, chunk, device, tokens=None):
+    """Config 3 CSR: nnz ~ Poisson(L0) per row, indices without replacement from Zipf(1.1)
+    over a random permutation (Gumbel-top-k), sorted; values |N(0,1)|*2."""
+    c = CONFIGS[cfg_id]
+    gen = torch.Generator(device=device).manual_seed(2_000_003 + chunk)
+    T = tokens or c["tokens"]
+    d_sae = c["d_sae"]
+    perm = torch.randperm(d_sae, generator=gen, device=device)
+    logp = torch.empty(d_sae, device=device)
+    logp[perm] = -1.1 * torch.log(torch.arange(1, d_sae + 1, device=device, dtype=torch.float32))
+    counts = torch.poisson(torch.full((T,), c["l0"], device=device), generator=gen).long().clamp(0, 256)
+    kmax = int(counts.max())
+    idx_rows = []
+    for r0 in range(0, T, 2048):
+        r1 = min(T, r0 + 2048)
+        u = torch.rand(r1 - r0, d_sae, generator=gen, device=device).clamp_(1e-12, 1 - 1e-7)
+        keys = logp - torch.log(-torch.log(u))
+        idx_rows.append(keys.topk(kmax, dim=1).indices)
+        del u, keys
+    top = torch.cat(idx_rows)  # [T, kmax] in key order
+    mask = torch.arange(kmax, device=device)[None, :] < counts[:, None]
+    sel = torch.where(mask, top, torch.full_like(top, d_sae))  # pad sorts last
+    sel = sel.sort(dim=1).values
+    indices = sel[mask.sort(dim=1, descending=True).values].to(torch.int32)
+    indptr = torch.zeros(T + 1, dtype=torch.int64, device=device)
+    indptr[1:] = counts.cumsum(0)
+    values = (torch.randn(indices.numel(), generator=gen, device=device).abs() * 2).to(c["dtype"])
+    return indptr, indices, values
+
+
+# ------------------------------------------------------------------------------ measurement helpers
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU's SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap,utilization.gpu")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.lines = []
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:  # noqa: BLE001
+            ident = str(device_index)
+        self.cmd = ["nvidia-smi", f"--id={ident}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "200"]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        rows = []
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[0]), max=float(parts[1]), util=float(parts[7]),
+                                 reasons=[n for n, v in zip(("hw_slowdown", "hw_thermal_slowdown",
+                                                             "sw_thermal_slowdown", "sw_power_cap"), parts[3:7])
+                                          if v.lower().startswith("active")]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        loaded = [r for r in rows if r["util"] >= 50] or rows
+        sms = sorted(r["sm"] for r in loaded)
+        reasons = sorted({x for r in loaded for x in r["reasons"]})
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(r["max"] for r in rows), "reasons": reasons,
+                "samples": len(rows), "samples_under_load": len(loaded)}
+
+
+def l2_flush(buf):
+    buf.add_(1)  # 256 MB read+write: evicts the 126 MB L2 between steps
+
+
+# ------------------------------------------------------------------------------ our arm
+
+def run_ours(args, rank, world, device):
+    from saeflow_b200 import forward
+    from saeflow_b200.kernels import dense_to_csr, device_error, fused_encode, sparse_decode, topk_encode
+
+    cfg_id = args.config
+    c = CONFIGS[cfg_id]
+    T = args.tokens or c["tokens"]
+    sae = make_sae(cfg_id, device)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    if cfg_id == 3:
+        csr = make_csr(cfg_id, rank, device, T)
+
+        def step(ev):
+            ev[0].record(stream)
+            out = sparse_decode(*csr, sae.W_dec, sae.b_dec)
+            ev[3].record(stream)
+            return out
+        launches_per_step = 1
+    elif cfg_id == 4:
+        x = make_tokens(cfg_id, rank, device, T)
+        indptr = torch.arange(0, T * c["k"] + 1, c["k"], device=device, dtype=torch.int64)
+
+        def step(ev):
+            ev[0].record(stream)
+            vals, idx = topk_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, c["k"])
+            ev[1].record(stream)
+            ev[2].record(stream)
+            out = sparse_decode(indptr, idx.view(-1), vals.view(-1), sae.W_dec, sae.b_dec)
+            ev[3].record(stream)
+            return out
+        launches_per_step = 4  # shift, encode+top-k, merge, decode
+    else:
+        x = make_tokens(cfg_id, rank, device, T)
+        row_nnz = torch.zeros(T, dtype=torch.int32, device=device)
+
+        def step(ev):
+            row_nnz.zero_()
+            ev[0].record(stream)
+            f = fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation, row_nnz=row_nnz)
+            ev[1].record(stream)
+            csr = dense_to_csr(f, row_nnz)
+            ev[2].record(stream)
+            out = sparse_decode(*csr, sae.W_dec, sae.b_dec)
+            ev[3].record(stream)
+            step.nnz = csr[1].numel()
+            del f
+            return out
+        launches_per_step = 5  # shift, encode, indptr scan, compact, decode
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for _ in range(args.warmup):
+        l2_flush(flush)
+        step([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+    barrier()
+    with ClockSampler(device.index) as clk:
+        barrier()
+        wall0 = time.perf_counter()
+        for i in range(args.steps):
+            l2_flush(flush)
+            step(events[i])
+        barrier()
+        wall = time.perf_counter() - wall0
+    step_ms = [e[0].elapsed_time(e[3]) for e in events]
+    enc_ms = [e[0].elapsed_time(e[1]) for e in events] if cfg_id != 3 else []
+    csr_ms = [e[1].elapsed_time(e[2]) for e in events] if cfg_id in (1, 2) else []
+    dec_ms = [e[2].elapsed_time(e[3]) for e in events] if cfg_id != 3 else step_ms
+    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)
+    total_ms = float(total_ms.item())
+
+    # ---- end to end through the public API with host buffers (H2D in, D2H out, per step)
+    e2e = None
+    if cfg_id in (1, 2, 4) and not args.no_e2e:
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty(T, c["d_in"], dtype=c["dtype"]).pin_memory()
+        e_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+
+        def e2e_step(ev):
+            ev[0].record(stream)
+            xd = x_host.to(device, non_blocking=True)
+            out = forward(sae, xd)
+            out_host.copy_(out, non_blocking=True)
+            ev[1].record(stream)
+
+        for _ in range(max(1, args.warmup)):
+            l2_flush(flush)
+            e2e_step([torch.cuda.Event(enable_timing=True) for _ in range(2)])
+        barrier()
+        for i in range(args.steps):
+            l2_flush(flush)
+            e2e_step(e_ev[i])
+        barrier()
+        e_tot = torch.tensor([sum(e[0].elapsed_time(e[1]) for e in e_ev)], dtype=torch.float64, device=device)
+        if world > 1:
+            torch.distributed.all_reduce(e_tot, op=torch.distributed.ReduceOp.MAX)
+        e_tot = float(e_tot.item())
+        nbytes = T * c["d_in"] * x.element_size()
+        e2e = {"value": round(world * T * args.steps / (e_tot / 1e3), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+               "ms_per_step": round(e_tot / args.steps, 4),
+               "api": "saeflow_b200.forward(sae, x) on pinned host x, result copied to pinned host"}
+
+    err = device_error(device)
+    if err:
+        raise RuntimeError(f"device error bits {err} after the timed region")
+
+    if rank != 0:
+        return None
+
+    peaks, peak_src = load_peaks()
+    mean = lambda v: sum(v) / len(v) if v else None  # noqa: E731
+    e = c["dtype"].itemsize if hasattr(c["dtype"], "itemsize") else torch.finfo(c["dtype"]).bits // 8
+    stages = {}
+    roofline = None
+    if cfg_id != 3:
+        flops = 2.0 * T * c["d_in"] * c["d_sae"]
+        enc = mean(enc_ms)
+        achieved = flops / (enc / 1e3) / 1e12
+        tc_peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        traffic = None
+        tp = ROOT / "profiles" / f"traffic_cfg{cfg_id}.json"
+        if tp.exists():
+            traffic = json.loads(tp.read_text()).get("encode_dram_bytes_per_launch")
+        roofline = {"kernel": "fused encode (shift pre-pass + tcgen05 GEMM + epilogue)" if cfg_id != 1
+                    else "fused encode (shift pre-pass + CUDA-core fp32 GEMM + epilogue)",
+                    "bound": "tensor", "achieved": round(achieved, 2), "peak": tc_peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / tc_peak, 4), "traffic": traffic,
+                    "peak_source": f"{peak_src} bf16_tflops (burst)",
+                    "algorithmic": f"2*T*d_in*d_sae = {flops:.4g} FLOP per launch"}
+        stages["encode_ms"] = round(enc, 4)
+        stages["encode_tflops"] = round(achieved, 2)
+    dec = mean(dec_ms)
+    if cfg_id in (1, 2):
+        stages["csr_ms"] = round(mean(csr_ms), 4)
+        nnz = step.nnz
+        l0 = nnz / T
+        comp_bytes = T * c["d_sae"] * e + nnz * (4 + e) + (T + 1) * 8
+        stages["csr_gbps"] = round(comp_bytes / (mean(csr_ms) / 1e3) / 1e9, 1)
+        stages["l0"] = round(l0, 2)
+    elif cfg_id == 3:
+        nnz = csr[1].numel()
+        l0 = nnz / T
+    else:
+        l0 = c["k"]
+        nnz = T * l0
+    dec_bytes = nnz * (c["d_in"] * e + 4 + e) + T * c["d_in"] * e + (T + 1) * 8
+    stages["decode_ms"] = round(dec, 4)
+    stages["decode_gbps_requested"] = round(dec_bytes / (dec / 1e3) / 1e9, 1)
+    if cfg_id == 3:
+        hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        roofline = {"kernel": "sparse decode (CSR gather)", "bound": "hbm",
+                    "achieved": stages["decode_gbps_requested"], "peak": hbm, "unit": "GB/s",
+                    "frac": round(stages["decode_gbps_requested"] / hbm, 4), "traffic": None,
+                    "peak_source": f"{peak_src} hbm_gbs",
+                    "algorithmic": "requested bytes L0*(d_in*e+4+e)+d_in*e+8 per token (bench_decode.py:57)"}
+
+    value = world * T * args.steps / (total_ms / 1e3)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if c["dtype"] == torch.bfloat16 else ("fp32" if c["dtype"] == torch.float32 else "fp16"),
+        "data": "synthetic (seeded, BASELINE config distributions)",
+        "config": {"workload": c["name"], "tokens_per_gpu": T, "global_batch": world * T,
+                   "parallelism": f"token-sharded x{world}, weights replicated, no data-path collective",
+                   "l2": "flushed between steps (256 MB write, outside the per-step events)"},
+        "impl": "ours",
+        "stages": stages,
+        "roofline": roofline,
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+        "wall_s_timed_region": round(wall, 3),
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(cfg_id, budget_s=args.cpu_seconds)
+    return line
+
+
+# ------------------------------------------------------------------------------ CPU (reference) arm
+
+def cpu_pipeline_setup(cfg_id, tokens):
+    """Weights and a token sample on the CPU, from the same generators (CPU RNG)."""
+    sae = make_sae(cfg_id, torch.device("cpu"))
+    import oracle
+
+    ref = oracle.RefSAE.__new__(oracle.RefSAE)
+    torch.nn.Module.__init__(ref)
+    ref.d_in, ref.d_sae, ref.activation, ref.k = sae.d_in, sae.d_sae, sae.activation, sae.k
+    for name in ("W_enc", "W_dec", "b_enc", "b_dec", "threshold"):
+        setattr(ref, name, getattr(sae, name))
+    ref.W_dec32, ref.b_dec32 = ref.W_dec.float(), ref.b_dec.float()
+    x = make_tokens(cfg_id if cfg_id != 3 else 2, 0, torch.device("cpu"), tokens)
+    return ref, x
+
+
+def cpu_step(ref, x):
+    """The reference's CPU path: dense SAE encode -> to_sparse_csr -> addmm(b_dec, csr, W_dec)
+    (saeflow/reference.py:36-46, bench/bench_decode.py:61-64,90). The CPU CSR addmm has no
+    bf16 kernel, so a 16-bit SAE decodes through fp32 copies of W_dec / b_dec made once at
+    set-up (`ref.W_dec32`) and the result is cast back."""
+    f = ref.encode(x)
+    csr = f.to_sparse_csr()
+    if ref.W_dec.dtype == torch.float32:
+        return torch.addmm(ref.b_dec.expand(x.shape[0], -1), csr, ref.W_dec)
+    csr32 = torch.sparse_csr_tensor(csr.crow_indices(), csr.col_indices(), csr.values().float(), csr.shape)
+    return torch.addmm(ref.b_dec32.expand(x.shape[0], -1), csr32, ref.W_dec32).to(ref.W_dec.dtype)
+
+
+def cpu_baseline(cfg_id, budget_s=10.0, sample_tokens=None):
+    cores = torch.get_num_threads()
+    ref, x = cpu_pipeline_setup(cfg_id, sample_tokens or (1024 if cfg_id != 1 else 4096))
+    cpu_step(ref, x[:64])  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        cpu_step(ref, x)
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n * x.shape[0] / dt, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} x {x.shape[0]} tokens of {CONFIGS[cfg_id]['name']} in {dt:.1f} s "
+                      "(oracle restatement of the reference CPU path: dense encode -> to_sparse_csr -> addmm)"}
+
+
+def run_reference(args):
+    cfg_id = args.config
+    c = CONFIGS[cfg_id]
+    sample = args.cpu_tokens
+    ref, x = cpu_pipeline_setup(cfg_id, sample)
+    for _ in range(args.warmup):
+        cpu_step(ref, x)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_step(ref, x)
+    dt = time.perf_counter() - t0
+    value = args.steps * sample / dt
+    cores = torch.get_num_threads()
+    desc = (f"{sample} tokens per step of {c['name']} on {cores} host threads "
+            "(oracle restatement of the reference CPU path: dense encode -> to_sparse_csr -> addmm)")
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if c["dtype"] == torch.bfloat16 else "fp32", "data": "synthetic (seeded)",
+        "config": {"workload": c["name"], "tokens_per_step": sample, "parallelism": "host CPU, rank 0 only"},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------------------------------ main
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default: the config's)")
+    ap.add_argument("--cpu-tokens", type=int, default=1024, help="reference arm: tokens per step")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline time budget")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args(argv)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return 0
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+    try:
+        line = run_ours(args, rank, world, device)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,172 @@
+/*
+ * saeflow_b200 — C ABI of the B200 (sm_100a) SAE hot path:
+ *
+ *     fused encode  ->  dense -> CSR compaction  ->  CSR sparse decode
+ *
+ * Every entry point takes plain device pointers, element strides, dtype codes and a
+ * CUDA stream, launches its kernels on that stream and returns an sf_status code.
+ * Nothing here synchronises the stream except sf_device_error(). No torch types cross
+ * this boundary; the Python layer in saeflow_b200/kernels binds it with ctypes.
+ *
+ * The reference interfaces these replace are the Triton host wrappers of saeflow:
+ *   saeflow/kernels/encode.py:97-139   fused_encode
+ *   saeflow/kernels/decode.py:77-94    dense_to_csr  (count, cumsum, host sync, compaction)
+ *   saeflow/kernels/decode.py:97-120   sparse_decode
+ *   saeflow/ops.py:12-16,29-36         TopK encode (dense ReLU encode + torch.topk)
+ * Each declaration below names the line range it replaces.
+ */
+#ifndef SAEFLOW_B200_H
+#define SAEFLOW_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SF_ABI_VERSION 1
+
+/* The library is built with hidden visibility; only these entry points are exported. */
+#if defined(__GNUC__)
+#define SF_API __attribute__((visibility("default")))
+#else
+#define SF_API
+#endif
+
+/* A cudaStream_t; 0 is the legacy default stream. */
+typedef struct CUstream_st *sf_stream;
+
+/* Element types. Codes are stable ABI. */
+enum sf_dtype { SF_F32 = 0, SF_BF16 = 1, SF_F16 = 2 };
+
+/* Activations of fused_encode (saeflow/kernels/encode.py:16 ACTIVATIONS). */
+enum sf_activation { SF_ACT_RELU = 0, SF_ACT_JUMPRELU = 1 };
+
+/* Return codes. SF_ERR_INVALID maps to Python ValueError, the rest to RuntimeError. */
+enum sf_status {
+    SF_OK = 0,
+    SF_ERR_INVALID = 1,      /* bad shape / dtype / pointer / stride combination     */
+    SF_ERR_UNSUPPORTED = 2,  /* valid request this build has no kernel for            */
+    SF_ERR_CUDA = 3,         /* a CUDA runtime or driver call failed                  */
+    SF_ERR_WORKSPACE = 4,    /* workspace pointer missing or smaller than required    */
+    SF_ERR_DEVICE = 5        /* a kernel reported a device-side error (sf_device_error) */
+};
+
+/* Encode variant selector (the `config=` kwarg of fused_encode).                  */
+enum sf_encode_variant {
+    SF_VARIANT_AUTO = 0,     /* tensor cores for 16-bit / TF32, CUDA cores for IEEE fp32 */
+    SF_VARIANT_TCGEN05 = 1,  /* force the tcgen05/TMEM kernel                        */
+    SF_VARIANT_SIMT = 2      /* force the CUDA-core kernel                           */
+};
+
+/* A strided 2-D tensor: element (i, j) is at data + (i*stride_row + j*stride_col)*size. */
+typedef struct sf_matrix {
+    const void *data;
+    int32_t dtype;           /* enum sf_dtype */
+    int32_t reserved;
+    int64_t rows, cols;
+    int64_t stride_row, stride_col;   /* in elements */
+} sf_matrix;
+
+/* A strided 1-D tensor; data == NULL means "absent" where the argument is optional. */
+typedef struct sf_vector {
+    const void *data;
+    int32_t dtype;
+    int32_t reserved;
+    int64_t len;
+    int64_t stride;          /* in elements */
+} sf_vector;
+
+/* Message of the last failing call on this host thread ("" if none). */
+SF_API const char *sf_last_error(void);
+
+/* ABI version (SF_ABI_VERSION) of the loaded library. */
+SF_API int sf_abi_version(void);
+
+/*
+ * Device-side error word of the current device: kernels never trap; a bounded wait
+ * that runs out, or an out-of-range CSR index, ORs a code into this word. The call
+ * synchronises the device, stores the word in *code and clears it.
+ * Bits: 1 = pipeline wait timed out, 2 = CSR index out of range, 4 = bad indptr.
+ */
+SF_API int sf_device_error(uint32_t *code);
+
+/*
+ * Workspace bytes sf_fused_encode needs for these operands (the b_dec-shifted,
+ * dtype-converted copy of x, plus a repacked W_enc when its layout cannot be read by
+ * TMA). Replaces the allocation-free Triton launch of saeflow/kernels/encode.py:115-139.
+ */
+SF_API int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int allow_tf32,
+                              int variant, size_t *bytes);
+
+/*
+ * out = act((x - b_dec) @ W_enc + b_enc), fp32 accumulation.
+ * Replaces saeflow/kernels/encode.py:97-139 (+ _encode_kernel :36-91).
+ *   x      [M, d_in]  f32/bf16/f16, any strides
+ *   W_enc  [d_in, d_sae], any strides; its dtype picks the MMA type (encode.py:72)
+ *   b_enc, b_dec, threshold: vectors (threshold only for SF_ACT_JUMPRELU)
+ *   out    [M, d_sae] in out->dtype, any strides (data is written through)
+ *   row_nnz: NULL or int32 [M]; each row's count of stored nonzeros is ADDED
+ *            (encode.py:89-91; the buffer is caller-zeroed)
+ *   allow_tf32: fp32 W_enc only; 0 = IEEE fp32 products (encode.py:118-120)
+ */
+SF_API int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
+                    const sf_vector *b_dec, const sf_vector *threshold, int activation,
+                    const sf_matrix *out, int32_t *row_nnz, int allow_tf32, int variant,
+                    void *workspace, size_t workspace_bytes, sf_stream stream);
+
+/*
+ * row_nnz[m] = number of f[m, :] != 0 (NaN counts, -0.0 does not). Overwrites.
+ * Replaces torch.count_nonzero at saeflow/kernels/decode.py:85.
+ */
+SF_API int sf_row_nnz(const sf_matrix *f, int32_t *row_nnz, sf_stream stream);
+
+/*
+ * indptr[0] = 0, indptr[m+1] = sum_{i<=m} row_nnz[i] (int64).
+ * Replaces saeflow/kernels/decode.py:86-87 (zeros + cumsum).
+ */
+SF_API int sf_csr_indptr(const int32_t *row_nnz, int64_t M, int64_t *indptr, sf_stream stream);
+
+/*
+ * Canonical (column-sorted) CSR of the nonzeros of f, given its indptr.
+ * indices int32 [nnz], values [nnz] in values_dtype (conversion from f's dtype if it
+ * differs). Replaces _compact_kernel, saeflow/kernels/decode.py:61-74,93.
+ */
+SF_API int sf_dense_to_csr(const sf_matrix *f, const int64_t *indptr, int32_t *indices, void *values,
+                    int values_dtype, sf_stream stream);
+
+/*
+ * out[m, :] = b_dec + sum_{j in row m} values[j] * W_dec[indices[j], :], fp32 accumulation.
+ * Replaces saeflow/kernels/decode.py:97-120 (+ _decode_kernel :28-55).
+ *   indptr int64 [M+1], indices int32 [nnz], values [nnz] (values_dtype)
+ *   W_dec [d_sae, d_in] any strides; b_dec NULL data = no bias; out [M, d_in] any strides.
+ * An index outside [0, d_sae) contributes nothing and sets bit 2 of the device error.
+ */
+SF_API int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *indices, const void *values,
+                     int values_dtype, const sf_matrix *W_dec, const sf_vector *b_dec,
+                     const sf_matrix *out, sf_stream stream);
+
+/*
+ * Workspace bytes for sf_topk_encode.
+ */
+SF_API int sf_topk_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int k, int allow_tf32,
+                             size_t *bytes);
+
+/*
+ * TopK SAE encode without the dense [M, d_sae] output: per row the k largest values of
+ * relu((x - b_dec) @ W_enc + b_enc), rounded to values_dtype, selected inside the GEMM
+ * epilogue. Output is fixed width: indices int32 [M, k], values [M, k], each row sorted
+ * by value descending, ties by lower feature index.
+ * Replaces saeflow/ops.py:12-16 (_topk) and :32-36 (TopK branch of encode_sparse).
+ */
+SF_API int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
+                   const sf_vector *b_dec, int k, int32_t *indices, void *values,
+                   int values_dtype, int allow_tf32, void *workspace, size_t workspace_bytes,
+                   sf_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SAEFLOW_B200_H */

@@ -1,0 +1,614 @@
+// extern "C" entry points of libsaeflow_b200.so: argument validation, workspace layout,
+// kernel selection. The entry points mirror the host wrappers of saeflow/kernels
+// (encode.py:97-139, decode.py:77-126) one level down: the caller owns every buffer.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "sf_common.cuh"
+#include "sf_internal.h"
+
+namespace sf {
+
+// Defined in sparse.cu
+int launch_row_nnz(const sf_matrix &f, int32_t *row_nnz, cudaStream_t s);
+int launch_indptr(const int32_t *cnt, int64_t M, int64_t *indptr, cudaStream_t s);
+int launch_compact(const sf_matrix &f, const int64_t *indptr, int32_t *indices, void *values, int vdt,
+                   cudaStream_t s);
+int launch_decode(const int64_t *indptr, int64_t M, const int32_t *indices, const void *values, int vdt,
+                  const sf_matrix &W, const sf_vector *b, const sf_matrix &out, cudaStream_t s);
+int launch_topk_merge(const unsigned long long *cand, int64_t M, int ncand, int k, int32_t *out_idx, void *out_val,
+                      int vdt, cudaStream_t s);
+
+namespace {
+thread_local char g_last_error[512] = "";
+
+// One error word per device, read back by sf_device_error().
+__device__ unsigned g_error_word;
+
+constexpr int kMaxDevices = 64;
+unsigned *g_error_ptr[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+std::mutex g_dev_mu;
+
+int current_device() {
+    int d = 0;
+    cudaGetDevice(&d);
+    return d;
+}
+}  // namespace
+
+int set_error(int status, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return status;
+}
+
+int check_cuda(cudaError_t e, const char *what) {
+    if (e == cudaSuccess) return SF_OK;
+    return set_error(SF_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+size_t dtype_size(int dtype) { return dtype == SF_F32 ? 4 : 2; }
+bool valid_dtype(int dtype) { return dtype == SF_F32 || dtype == SF_BF16 || dtype == SF_F16; }
+
+unsigned *device_error_word() {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!g_error_ptr[d]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_error_word) == cudaSuccess) g_error_ptr[d] = static_cast<unsigned *>(p);
+    }
+    return g_error_ptr[d];
+}
+
+int num_sms() {
+    const int d = current_device();
+    if (d < 0 || d >= kMaxDevices) return 148;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!g_sms[d]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d) != cudaSuccess || n <= 0) n = 148;
+        g_sms[d] = n;
+    }
+    return g_sms[d];
+}
+
+namespace {
+
+// ------------------------------------------------------------------ pre-pass kernels
+// xs[m, k] = MT(float(x[m, k]) - float(b_dec[k])) for k < K, 0 for K <= k < pitch.
+// Rounding to the MMA dtype after an fp32 subtraction is the reference prologue
+// (saeflow/kernels/encode.py:72 of _encode_kernel).
+template <typename XT, typename MT>
+__global__ void shift_convert_kernel(const XT *__restrict__ x, int64_t M, int64_t K, int64_t sxm, int64_t sxk,
+                                     const void *b_dec, int b_dtype, int64_t b_stride, MT *__restrict__ xs,
+                                     int64_t pitch) {
+    constexpr int EPV = 16 / sizeof(MT);
+    const int64_t vec_per_row = pitch / EPV;
+    const int64_t total = M * vec_per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / vec_per_row;
+        const int64_t k0 = (i - m * vec_per_row) * EPV;
+        uint4 pk;
+        MT *o = reinterpret_cast<MT *>(&pk);
+        const XT *xr = x + m * sxm;
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) {
+            const int64_t k = k0 + e;
+            float v = 0.f;
+            if (k < K) {
+                v = to_f32(xr[k * sxk]);
+                if (b_dec) v -= load_as_f32(b_dec, b_dtype, k * b_stride);
+            }
+            o[e] = from_f32<MT>(k < K ? v : 0.f);
+        }
+        *reinterpret_cast<uint4 *>(xs + m * pitch + k0) = pk;
+    }
+}
+
+// Contiguous fast path: 16-byte loads of x (x rows contiguous, K multiple of EPV_X).
+template <typename XT, typename MT>
+__global__ void shift_convert_vec_kernel(const XT *__restrict__ x, int64_t M, int64_t K, int64_t sxm,
+                                         const void *b_dec, int b_dtype, int64_t b_stride, MT *__restrict__ xs,
+                                         int64_t pitch) {
+    constexpr int EPV = 8;  // elements per work item (16 B of 16-bit, 32 B of fp32)
+    const int64_t items_per_row = pitch / EPV;
+    const int64_t total = M * items_per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / items_per_row;
+        const int64_t k0 = (i - m * items_per_row) * EPV;
+        float v[EPV];
+        if (k0 + EPV <= K) {
+            const XT *src = x + m * sxm + k0;
+            if (sizeof(XT) == 2) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4 *>(src));
+                const XT *e = reinterpret_cast<const XT *>(&q);
+#pragma unroll
+                for (int t = 0; t < EPV; ++t) v[t] = to_f32(e[t]);
+            } else {
+                const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(src));
+                const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(src) + 1);
+                const XT *e0 = reinterpret_cast<const XT *>(&q0);
+                const XT *e1 = reinterpret_cast<const XT *>(&q1);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) v[t] = to_f32(e0[t]), v[t + 4] = to_f32(e1[t]);
+            }
+#pragma unroll
+            for (int t = 0; t < EPV; ++t)
+                if (b_dec) v[t] -= load_as_f32(b_dec, b_dtype, (k0 + t) * b_stride);
+        } else {
+#pragma unroll
+            for (int t = 0; t < EPV; ++t) {
+                const int64_t k = k0 + t;
+                v[t] = k < K ? to_f32(x[m * sxm + k]) - (b_dec ? load_as_f32(b_dec, b_dtype, k * b_stride) : 0.f)
+                             : 0.f;
+            }
+        }
+        MT *dst = xs + m * pitch + k0;
+        if (sizeof(MT) == 2) {
+            uint4 pk;
+            MT *o = reinterpret_cast<MT *>(&pk);
+#pragma unroll
+            for (int t = 0; t < EPV; ++t) o[t] = from_f32<MT>(v[t]);
+            *reinterpret_cast<uint4 *>(dst) = pk;
+        } else {
+            float4 *d4 = reinterpret_cast<float4 *>(dst);
+            d4[0] = make_float4(v[0], v[1], v[2], v[3]);
+            d4[1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+    }
+}
+
+// wp[k, n] = W[k, n] (row pitch `pitch`, zero padding) — makes any W_enc layout TMA-readable.
+template <typename T>
+__global__ void repack_kernel(const T *__restrict__ W, int64_t K, int64_t N, int64_t swk, int64_t swn,
+                              T *__restrict__ wp, int64_t pitch) {
+    const int64_t total = K * pitch;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t k = i / pitch, n = i - k * pitch;
+        wp[i] = n < N ? W[k * swk + n * swn] : from_f32<T>(0.f);
+    }
+}
+
+// wt[n, k] = W[k, n] (row pitch `pitch` >= K, zero padding): K-major copy of W_enc for
+// the TF32 path, whose 32-bit operands the tensor cores read K-major. 32 x 32 tiles
+// through shared memory so both the read and the write are coalesced.
+template <typename T>
+__global__ void repack_t_kernel(const T *__restrict__ W, int64_t K, int64_t N, int64_t swk, int64_t swn,
+                                T *__restrict__ wt, int64_t pitch) {
+    __shared__ T tile[32][33];
+    const int64_t n0 = (int64_t)blockIdx.x * 32, k0 = (int64_t)blockIdx.y * 32;
+    const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t k = k0 + i, n = n0 + tx;
+        tile[i][tx] = (k < K && n < N) ? W[k * swk + n * swn] : from_f32<T>(0.f);
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t n = n0 + i, k = k0 + tx;
+        if (n < N && k < pitch) wt[n * pitch + k] = tile[tx][i];
+    }
+}
+
+template <typename F>
+int by_dtype2(int dt, F &&f) {
+    if (dt == SF_F32) return f(float{});
+    if (dt == SF_BF16) return f(__nv_bfloat16{});
+    return f(__half{});
+}
+
+unsigned grid_for(int64_t items) {
+    const int64_t per = 256;
+    int64_t blocks = (items + per - 1) / per;
+    const int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (unsigned)blocks;
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+// ------------------------------------------------------------------ validation
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_matrix(const sf_matrix *m, const char *name) {
+    if (!m) return set_error(SF_ERR_INVALID, "%s is NULL", name);
+    if (!valid_dtype(m->dtype)) return set_error(SF_ERR_INVALID, "%s has unsupported dtype code %d", name, m->dtype);
+    if (m->rows < 0 || m->cols < 0) return set_error(SF_ERR_INVALID, "%s has a negative extent", name);
+    if (m->rows > 0 && m->cols > 0 && !m->data) return set_error(SF_ERR_INVALID, "%s has no data", name);
+    if (m->rows > (int64_t)INT32_MAX || m->cols > (int64_t)INT32_MAX)
+        return set_error(SF_ERR_UNSUPPORTED, "%s extent exceeds 2^31-1", name);
+    return SF_OK;
+}
+
+int check_vector(const sf_vector *v, int64_t len, const char *name, bool optional) {
+    if (!v || !v->data) {
+        if (optional) return SF_OK;
+        return set_error(SF_ERR_INVALID, "%s is required", name);
+    }
+    if (!valid_dtype(v->dtype)) return set_error(SF_ERR_INVALID, "%s has unsupported dtype code %d", name, v->dtype);
+    if (v->len != len)
+        return set_error(SF_ERR_INVALID, "%s has length %lld, expected %lld", name, (long long)v->len, (long long)len);
+    return SF_OK;
+}
+
+// MMA type from W_enc's dtype and the TF32 switch (encode.py:118-120: fp32 inputs use
+// IEEE products unless TF32 is allowed; any 16-bit input forces the tensor-core path).
+struct EncodePlan {
+    bool tensor_cores;
+    int ab_fmt;      // 0 f16, 1 bf16, 2 tf32
+    int mma_dtype;   // storage dtype of the shifted x copy
+    int64_t a_pitch;
+    bool w_direct;   // TMA reads W_enc in place
+    bool b_mn;
+    int64_t w_pitch; // pitch of W_enc as TMA sees it (elements)
+    size_t xs_bytes, wp_bytes;
+};
+
+int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int variant, EncodePlan *pl) {
+    const int64_t M = x->rows, K = x->cols, N = W->cols;
+    const int wdt = W->dtype;
+    if (variant < SF_VARIANT_AUTO || variant > SF_VARIANT_SIMT)
+        return set_error(SF_ERR_INVALID, "unknown encode variant %d", variant);
+    bool tc;
+    if (wdt == SF_F32) {
+        const bool tf32 = allow_tf32 || x->dtype != SF_F32;
+        tc = tf32;
+        if (variant == SF_VARIANT_TCGEN05) tc = true;
+        if (variant == SF_VARIANT_SIMT) tc = false;
+    } else {
+        tc = true;
+        if (variant == SF_VARIANT_SIMT)
+            return set_error(SF_ERR_UNSUPPORTED, "the CUDA-core encode kernel is fp32 only");
+    }
+    pl->tensor_cores = tc;
+    pl->mma_dtype = wdt;
+    pl->ab_fmt = wdt == SF_F32 ? 2 : (wdt == SF_BF16 ? 1 : 0);
+    const int64_t es = (int64_t)dtype_size(wdt);
+    const int64_t epv = 16 / es;
+    // Shifted x: rows padded to 16 B (vector kernel writes 8 elements per item).
+    pl->a_pitch = round_up(K > 0 ? K : 1, 8);
+    pl->xs_bytes = (size_t)(M * pl->a_pitch * es);
+    pl->wp_bytes = 0;
+    pl->w_direct = true;
+    pl->b_mn = true;
+    pl->w_pitch = 0;
+    if (tc && wdt == SF_F32) {
+        // 32-bit operands: feed W_enc K-major (in place when it is column-major).
+        pl->b_mn = false;
+        if (W->stride_row == 1 && (W->stride_col * es) % 16 == 0 && aligned16(W->data) && W->stride_col >= K) {
+            pl->w_pitch = W->stride_col;
+        } else {
+            pl->w_direct = false;
+            pl->w_pitch = round_up(K > 0 ? K : 1, epv);
+            pl->wp_bytes = (size_t)(N * pl->w_pitch * es);
+        }
+    } else if (tc) {
+        const bool al = aligned16(W->data);
+        if (W->stride_col == 1 && (W->stride_row * es) % 16 == 0 && al && W->stride_row >= N) {
+            pl->b_mn = true;
+            pl->w_pitch = W->stride_row;
+        } else if (W->stride_row == 1 && (W->stride_col * es) % 16 == 0 && al && W->stride_col >= K) {
+            pl->b_mn = false;
+            pl->w_pitch = W->stride_col;
+        } else {
+            pl->w_direct = false;
+            pl->b_mn = true;
+            pl->w_pitch = round_up(N > 0 ? N : 1, epv);
+            pl->wp_bytes = (size_t)(K * pl->w_pitch * es);
+        }
+    }
+    return SF_OK;
+}
+
+size_t plan_workspace(const EncodePlan &pl) { return round_up((int64_t)pl.xs_bytes, 256) + pl.wp_bytes; }
+
+int run_shift_convert(const sf_matrix *x, const sf_vector *b_dec, int mdt, void *xs, int64_t pitch, cudaStream_t s) {
+    const int64_t M = x->rows, K = x->cols;
+    if (M == 0) return SF_OK;
+    const void *bp = (b_dec && b_dec->data) ? b_dec->data : nullptr;
+    const int bdt = bp ? b_dec->dtype : 0;
+    const int64_t bs = bp ? b_dec->stride : 0;
+    return by_dtype2(x->dtype, [&](auto xtag) {
+        using XT = decltype(xtag);
+        return by_dtype2(mdt, [&](auto mtag) {
+            using MT = decltype(mtag);
+            const int64_t xe = sizeof(XT);
+            const bool vec = x->stride_col == 1 && (x->stride_row * xe) % 16 == 0 && aligned16(x->data) &&
+                             (K % (16 / xe)) == 0;
+            if (vec) {
+                const int64_t items = M * (pitch / 8);
+                shift_convert_vec_kernel<XT, MT><<<grid_for(items), 256, 0, s>>>(
+                    reinterpret_cast<const XT *>(x->data), M, K, x->stride_row, bp, bdt, bs,
+                    reinterpret_cast<MT *>(xs), pitch);
+            } else {
+                const int64_t items = M * (pitch / (16 / (int64_t)sizeof(MT)));
+                shift_convert_kernel<XT, MT><<<grid_for(items), 256, 0, s>>>(
+                    reinterpret_cast<const XT *>(x->data), M, K, x->stride_row, x->stride_col, bp, bdt, bs,
+                    reinterpret_cast<MT *>(xs), pitch);
+            }
+            return check_cuda(cudaGetLastError(), "shift_convert launch");
+        });
+    });
+}
+
+int run_repack(const sf_matrix *W, void *wp, int64_t pitch, bool mn_major, cudaStream_t s) {
+    const int64_t K = W->rows, N = W->cols;
+    return by_dtype2(W->dtype, [&](auto tag) {
+        using T = decltype(tag);
+        if (!mn_major) {
+            dim3 grid((unsigned)((N + 31) / 32), (unsigned)((pitch + 31) / 32));
+            repack_t_kernel<T><<<grid, dim3(32, 8), 0, s>>>(reinterpret_cast<const T *>(W->data), K, N,
+                                                            W->stride_row, W->stride_col, reinterpret_cast<T *>(wp),
+                                                            pitch);
+            return check_cuda(cudaGetLastError(), "repack launch");
+        }
+        repack_kernel<T><<<grid_for(K * pitch), 256, 0, s>>>(reinterpret_cast<const T *>(W->data), K, N,
+                                                             W->stride_row, W->stride_col, reinterpret_cast<T *>(wp),
+                                                             pitch);
+        return check_cuda(cudaGetLastError(), "repack launch");
+    });
+}
+
+}  // namespace
+}  // namespace sf
+
+using namespace sf;
+
+extern "C" {
+
+const char *sf_last_error(void) { return g_last_error; }
+
+int sf_abi_version(void) { return SF_ABI_VERSION; }
+
+int sf_device_error(uint32_t *code) {
+    if (!code) return set_error(SF_ERR_INVALID, "code is NULL");
+    *code = 0;
+    unsigned *w = device_error_word();
+    if (!w) return set_error(SF_ERR_CUDA, "device error word unavailable");
+    int st = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    if (st) return st;
+    unsigned v = 0;
+    st = check_cuda(cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost), "read device error word");
+    if (st) return st;
+    const unsigned zero = 0;
+    st = check_cuda(cudaMemcpy(w, &zero, sizeof(zero), cudaMemcpyHostToDevice), "clear device error word");
+    if (st) return st;
+    *code = v;
+    return SF_OK;
+}
+
+int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int allow_tf32, int variant,
+                              size_t *bytes) {
+    if (!bytes) return set_error(SF_ERR_INVALID, "bytes is NULL");
+    *bytes = 0;
+    int st = check_matrix(x, "x");
+    if (!st) st = check_matrix(W_enc, "W_enc");
+    if (st) return st;
+    if (x->cols != W_enc->rows)
+        return set_error(SF_ERR_INVALID, "x has d_in=%lld but W_enc has d_in=%lld", (long long)x->cols,
+                         (long long)W_enc->rows);
+    EncodePlan pl;
+    st = plan_encode(x, W_enc, allow_tf32, variant, &pl);
+    if (st) return st;
+    *bytes = plan_workspace(pl);
+    return SF_OK;
+}
+
+int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc, const sf_vector *b_dec,
+                    const sf_vector *threshold, int activation, const sf_matrix *out, int32_t *row_nnz,
+                    int allow_tf32, int variant, void *workspace, size_t workspace_bytes, sf_stream stream) {
+    int st = check_matrix(x, "x");
+    if (!st) st = check_matrix(W_enc, "W_enc");
+    if (!st) st = check_matrix(out, "out");
+    if (st) return st;
+    const int64_t M = x->rows, K = x->cols, N = W_enc->cols;
+    if (activation != SF_ACT_RELU && activation != SF_ACT_JUMPRELU)
+        return set_error(SF_ERR_INVALID, "unknown activation code %d", activation);
+    if (K != W_enc->rows)
+        return set_error(SF_ERR_INVALID, "x has d_in=%lld but W_enc has d_in=%lld", (long long)K,
+                         (long long)W_enc->rows);
+    if (out->rows != M || out->cols != N)
+        return set_error(SF_ERR_INVALID, "out must be [%lld, %lld]", (long long)M, (long long)N);
+    st = check_vector(b_enc, N, "b_enc", false);
+    if (!st) st = check_vector(b_dec, K, "b_dec", true);
+    if (!st) st = check_vector(threshold, N, "threshold", activation != SF_ACT_JUMPRELU);
+    if (st) return st;
+    if (M == 0 || N == 0) return SF_OK;
+
+    EncodePlan pl;
+    st = plan_encode(x, W_enc, allow_tf32, variant, &pl);
+    if (st) return st;
+    const size_t need = plan_workspace(pl);
+    if (workspace_bytes < need || (!workspace && need))
+        return set_error(SF_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if (!aligned16(workspace)) return set_error(SF_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    void *xs = ws;
+    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
+    st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
+    if (st) return st;
+
+    EpilogueArgs ep{};
+    ep.b_enc = b_enc->data;
+    ep.b_enc_dtype = b_enc->dtype;
+    ep.b_enc_stride = b_enc->stride;
+    if (threshold && threshold->data) {
+        ep.thr = threshold->data;
+        ep.thr_dtype = threshold->dtype;
+        ep.thr_stride = threshold->stride;
+    }
+    ep.activation = activation;
+    ep.out = const_cast<void *>(out->data);
+    ep.out_dtype = out->dtype;
+    ep.out_sm = out->stride_row;
+    ep.out_sn = out->stride_col;
+    ep.out_vec = (out->stride_col == 1 && (out->stride_row * (int64_t)dtype_size(out->dtype)) % 16 == 0 &&
+                  aligned16(out->data))
+                     ? 1
+                     : 0;
+    ep.row_nnz = row_nnz;
+
+    if (!pl.tensor_cores)
+        return encode_simt_f32(static_cast<const float *>(xs), pl.a_pitch, static_cast<const float *>(W_enc->data),
+                               W_enc->stride_row, W_enc->stride_col, M, N, K, ep, s);
+
+    GemmOperands g{};
+    g.a = xs;
+    g.a_pitch = pl.a_pitch;
+    g.ab_fmt = pl.ab_fmt;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.b_mn_major = pl.b_mn;
+    if (pl.w_direct) {
+        g.b = W_enc->data;
+        g.b_pitch = pl.w_pitch;
+    } else {
+        st = run_repack(W_enc, wp, pl.w_pitch, pl.b_mn, s);
+        if (st) return st;
+        g.b = wp;
+        g.b_pitch = pl.w_pitch;
+    }
+    return encode_tc_dense(g, ep, s);
+}
+
+int sf_row_nnz(const sf_matrix *f, int32_t *row_nnz, sf_stream stream) {
+    int st = check_matrix(f, "f");
+    if (st) return st;
+    if (f->rows > 0 && !row_nnz) return set_error(SF_ERR_INVALID, "row_nnz is NULL");
+    if (f->cols == 0) {
+        if (f->rows) {
+            st = check_cuda(cudaMemsetAsync(row_nnz, 0, (size_t)f->rows * 4, reinterpret_cast<cudaStream_t>(stream)),
+                            "memset row_nnz");
+        }
+        return st;
+    }
+    return launch_row_nnz(*f, row_nnz, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int sf_csr_indptr(const int32_t *row_nnz, int64_t M, int64_t *indptr, sf_stream stream) {
+    if (M < 0) return set_error(SF_ERR_INVALID, "M is negative");
+    if (!indptr || (M > 0 && !row_nnz)) return set_error(SF_ERR_INVALID, "NULL pointer");
+    return launch_indptr(row_nnz, M, indptr, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int sf_dense_to_csr(const sf_matrix *f, const int64_t *indptr, int32_t *indices, void *values, int values_dtype,
+                    sf_stream stream) {
+    int st = check_matrix(f, "f");
+    if (st) return st;
+    if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
+    if (f->rows > 0 && !indptr) return set_error(SF_ERR_INVALID, "indptr is NULL");
+    if (f->rows == 0 || f->cols == 0) return SF_OK;
+    return launch_compact(*f, indptr, indices, values, values_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *indices, const void *values, int values_dtype,
+                     const sf_matrix *W_dec, const sf_vector *b_dec, const sf_matrix *out, sf_stream stream) {
+    int st = check_matrix(W_dec, "W_dec");
+    if (!st) st = check_matrix(out, "out");
+    if (st) return st;
+    if (M < 0) return set_error(SF_ERR_INVALID, "M is negative");
+    if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
+    if (out->rows != M || out->cols != W_dec->cols)
+        return set_error(SF_ERR_INVALID, "out must be [%lld, %lld]", (long long)M, (long long)W_dec->cols);
+    st = check_vector(b_dec, W_dec->cols, "b_dec", true);
+    if (st) return st;
+    if (M > 0 && !indptr) return set_error(SF_ERR_INVALID, "indptr is NULL");
+    const sf_vector *b = (b_dec && b_dec->data) ? b_dec : nullptr;
+    return launch_decode(indptr, M, indices, values, values_dtype, *W_dec, b, *out,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+int sf_topk_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int k, int allow_tf32, size_t *bytes) {
+    if (!bytes) return set_error(SF_ERR_INVALID, "bytes is NULL");
+    *bytes = 0;
+    int st = check_matrix(x, "x");
+    if (!st) st = check_matrix(W_enc, "W_enc");
+    if (st) return st;
+    if (k < 1 || k > W_enc->cols) return set_error(SF_ERR_INVALID, "k=%d must be in [1, d_sae=%lld]", k, (long long)W_enc->cols);
+    EncodePlan pl;
+    st = plan_encode(x, W_enc, 1, SF_VARIANT_TCGEN05, &pl);
+    if (st) return st;
+    (void)allow_tf32;
+    const int chunks = topk_chunks(x->rows, W_enc->cols);
+    *bytes = plan_workspace(pl) + 256 + (size_t)x->rows * chunks * k * sizeof(unsigned long long);
+    return SF_OK;
+}
+
+int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc, const sf_vector *b_dec, int k,
+                   int32_t *indices, void *values, int values_dtype, int allow_tf32, void *workspace,
+                   size_t workspace_bytes, sf_stream stream) {
+    int st = check_matrix(x, "x");
+    if (!st) st = check_matrix(W_enc, "W_enc");
+    if (st) return st;
+    const int64_t M = x->rows, K = x->cols, N = W_enc->cols;
+    if (K != W_enc->rows)
+        return set_error(SF_ERR_INVALID, "x has d_in=%lld but W_enc has d_in=%lld", (long long)K,
+                         (long long)W_enc->rows);
+    if (k < 1 || k > N) return set_error(SF_ERR_INVALID, "k=%d must be in [1, d_sae=%lld]", k, (long long)N);
+    if (k > kTopkMaxK) return set_error(SF_ERR_UNSUPPORTED, "fused top-k supports k <= %d", kTopkMaxK);
+    if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
+    st = check_vector(b_enc, N, "b_enc", false);
+    if (!st) st = check_vector(b_dec, K, "b_dec", true);
+    if (st) return st;
+    if (M == 0) return SF_OK;
+    if (!indices || !values) return set_error(SF_ERR_INVALID, "indices/values are NULL");
+    (void)allow_tf32;  // fp32 W_enc always runs this path on TF32 tensor cores
+
+    EncodePlan pl;
+    st = plan_encode(x, W_enc, 1, SF_VARIANT_TCGEN05, &pl);
+    if (st) return st;
+    const int chunks = topk_chunks(M, N);
+    const size_t base = plan_workspace(pl);
+    const size_t cand_off = (size_t)round_up((int64_t)base, 256);
+    const size_t need = cand_off + (size_t)M * chunks * k * sizeof(unsigned long long);
+    if (workspace_bytes < need || !workspace)
+        return set_error(SF_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if (!aligned16(workspace)) return set_error(SF_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    void *xs = ws;
+    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
+    auto *cand = reinterpret_cast<unsigned long long *>(ws + cand_off);
+
+    st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
+    if (st) return st;
+    GemmOperands g{};
+    g.a = xs;
+    g.a_pitch = pl.a_pitch;
+    g.ab_fmt = pl.ab_fmt;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.b_mn_major = pl.b_mn;
+    if (pl.w_direct) {
+        g.b = W_enc->data;
+        g.b_pitch = pl.w_pitch;
+    } else {
+        st = run_repack(W_enc, wp, pl.w_pitch, pl.b_mn, s);
+        if (st) return st;
+        g.b = wp;
+        g.b_pitch = pl.w_pitch;
+    }
+    TopkArgs tk{};
+    tk.b_enc = b_enc->data;
+    tk.b_enc_dtype = b_enc->dtype;
+    tk.b_enc_stride = b_enc->stride;
+    tk.k = k;
+    tk.values_dtype = values_dtype;
+    tk.n_chunks = chunks;
+    tk.cand = cand;
+    st = encode_tc_topk(g, tk, s);
+    if (st) return st;
+    return launch_topk_merge(cand, M, chunks * k, k, indices, values, values_dtype, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,166 @@
+// fp32 SAE encoder on the CUDA cores, IEEE fp32 products and fp32 accumulation.
+//
+// The reference computes fp32 inputs with `input_precision="ieee"` unless TF32 is
+// allowed (saeflow/kernels/encode.py:118-120); this kernel is that path. Epilogue
+// semantics are identical to the tensor-core kernel (encode.py:195-208).
+//
+// 128 x 128 output tile per CTA, K in steps of 8 through double-buffered shared memory,
+// 256 threads each owning an 8 x 8 register block (rows {4ty..4ty+3, 64+4ty..}, columns
+// {4tx..4tx+3, 64+4tx..}) so the shared-memory reads are conflict-free float4 broadcasts.
+#include "sf_common.cuh"
+#include "sf_internal.h"
+
+namespace sf {
+
+namespace {
+
+constexpr int SB_M = 128, SB_N = 128, SB_K = 8, SB_T = 256;
+
+template <typename OT>
+__device__ __forceinline__ void simt_store4(void *out, int64_t sm, int64_t sn, int vec, int64_t N, int row, int col,
+                                            const float (&v)[4]) {
+    OT *base = reinterpret_cast<OT *>(out) + (int64_t)row * sm;
+    if (vec && col + 4 <= N && sizeof(OT) == 4) {
+        *reinterpret_cast<float4 *>(base + col) = make_float4(v[0], v[1], v[2], v[3]);
+        return;
+    }
+    if (vec && col + 4 <= N && sizeof(OT) == 2) {
+        uint2 pk;
+        OT *e = reinterpret_cast<OT *>(&pk);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) e[j] = from_f32<OT>(v[j]);
+        *reinterpret_cast<uint2 *>(base + col) = pk;
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        if (col + j < N) base[(int64_t)(col + j) * sn] = from_f32<OT>(v[j]);
+}
+
+__global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restrict__ xs, int64_t ldx,
+                                                          const float *__restrict__ W, int64_t swk, int64_t swn,
+                                                          int M, int N, int K, EpilogueArgs ep, int w_vec) {
+    __shared__ __align__(16) float As[2][SB_K][SB_M + 4];
+    __shared__ __align__(16) float Bs[2][SB_K][SB_N + 4];
+    __shared__ float s_bias[SB_N], s_thr[SB_N];
+
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * SB_M, n0 = blockIdx.x * SB_N;
+
+    for (int j = tid; j < SB_N; j += SB_T) {
+        const int col = n0 + j;
+        s_bias[j] = col < N ? load_as_f32(ep.b_enc, ep.b_enc_dtype, (int64_t)col * ep.b_enc_stride) : 0.f;
+        s_thr[j] = (col < N && ep.activation == SF_ACT_JUMPRELU)
+                       ? load_as_f32(ep.thr, ep.thr_dtype, (int64_t)col * ep.thr_stride)
+                       : 0.f;
+    }
+
+    // Global -> register staging: A: row = tid/2, k-quad = tid%2; B: k = tid/32, n-quad = tid%32.
+    const int a_row = tid >> 1, a_kq = (tid & 1) * 4;
+    const int b_k = tid >> 5, b_nq = (tid & 31) * 4;
+    float4 ra;
+    float rb[4];
+
+    auto load_tile = [&](int k0) {
+        const int gr = m0 + a_row, gk = k0 + a_kq;
+        // xs rows are zero-padded to a multiple of 4 columns, so a quad never straddles K.
+        ra = (gr < M && gk < K) ? *reinterpret_cast<const float4 *>(xs + (int64_t)gr * ldx + gk)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        const int kk = k0 + b_k;
+        const int nn = n0 + b_nq;
+        if (w_vec && kk < K && nn + 4 <= N) {
+            const float4 t = *reinterpret_cast<const float4 *>(W + (int64_t)kk * swk + nn);
+            rb[0] = t.x, rb[1] = t.y, rb[2] = t.z, rb[3] = t.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                rb[j] = (kk < K && nn + j < N) ? __ldg(W + (int64_t)kk * swk + (int64_t)(nn + j) * swn) : 0.f;
+        }
+    };
+    auto store_tile = [&](int buf) {
+        As[buf][a_kq + 0][a_row] = ra.x;
+        As[buf][a_kq + 1][a_row] = ra.y;
+        As[buf][a_kq + 2][a_row] = ra.z;
+        As[buf][a_kq + 3][a_row] = ra.w;
+        *reinterpret_cast<float4 *>(&Bs[buf][b_k][b_nq]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+
+    const int nk = (K + SB_K - 1) / SB_K;
+    load_tile(0);
+    store_tile(0);
+    __syncthreads();
+    for (int kt = 0; kt < nk; ++kt) {
+        const int buf = kt & 1;
+        if (kt + 1 < nk) load_tile((kt + 1) * SB_K);
+#pragma unroll
+        for (int kk = 0; kk < SB_K; ++kk) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 + tx * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        if (kt + 1 < nk) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+
+    // Epilogue: bias, activation, rounding to the output dtype, count, store.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = (i < 4) ? ty * 4 + i : 64 + ty * 4 + (i - 4);
+        const int row = m0 + r;
+        int cnt = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int c = h * 64 + tx * 4;
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float pre = acc[i][h * 4 + j] + s_bias[c + j];
+                float o = fmaxf(pre, 0.f);
+                if (ep.activation == SF_ACT_JUMPRELU) o = (pre > s_thr[c + j]) ? o : 0.f;
+                o = round_to(o, ep.out_dtype);
+                v[j] = o;
+                cnt += (o != 0.f && n0 + c + j < N) ? 1 : 0;
+            }
+            if (row < M) {
+                if (ep.out_dtype == SF_F32)
+                    simt_store4<float>(ep.out, ep.out_sm, ep.out_sn, ep.out_vec, N, row, n0 + c, v);
+                else if (ep.out_dtype == SF_BF16)
+                    simt_store4<__nv_bfloat16>(ep.out, ep.out_sm, ep.out_sn, ep.out_vec, N, row, n0 + c, v);
+                else
+                    simt_store4<__half>(ep.out, ep.out_sm, ep.out_sn, ep.out_vec, N, row, n0 + c, v);
+            }
+        }
+        // The 16 threads sharing these rows are 16 consecutive lanes (same ty).
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+        if (tx == 0 && ep.row_nnz != nullptr && row < M && cnt != 0) atomicAdd(ep.row_nnz + row, cnt);
+    }
+}
+
+}  // namespace
+
+int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
+                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream) {
+    if ((N + SB_N - 1) / SB_N > 2147483647ll || (M + SB_M - 1) / SB_M > 65535)
+        return set_error(SF_ERR_UNSUPPORTED, "SIMT encode grid too large (M=%lld N=%lld)", (long long)M, (long long)N);
+    const int w_vec = (swn == 1 && (swk % 4) == 0 && (reinterpret_cast<uintptr_t>(W) & 15u) == 0) ? 1 : 0;
+    dim3 grid((unsigned)((N + SB_N - 1) / SB_N), (unsigned)((M + SB_M - 1) / SB_M));
+    encode_simt_kernel<<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec);
+    return check_cuda(cudaGetLastError(), "encode_simt launch");
+}
+
+}  // namespace sf

@@ -1,0 +1,577 @@
+// Fused SAE encoder on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+//
+//   out = act((x - b_dec) @ W_enc + b_enc)       fp32 accumulation in TMEM
+//
+// Follows the semantics of saeflow/kernels/encode.py:36-91 (_encode_kernel): the b_dec
+// shift is applied in fp32 and rounded to W_enc's dtype before the product (encode.py:72
+// of the kernel body, line 189 of the file), bias + ReLU / JumpReLU (strict `pre > thr`)
+// run on the fp32 accumulator (:195-199), and the epilogue adds each row's count of
+// stored nonzeros into row_nnz (:206-208). The count is taken on the value as stored
+// (after rounding to the output dtype), so it always equals count_nonzero(out).
+//
+// Design (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: x tile [128 x 128 B] and W tile [256 x 128 B] per stage,
+//               SWIZZLE_128B, 4-stage mbarrier ring, no multicast.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, M=128 N=256, fp32
+//               accumulators double-buffered in TMEM (2 x 256 columns).
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, bias/activation in fp32,
+//               rounding, nonzero count, 16-byte streaming stores (L2 evict_first).
+//               In TOPK mode they instead keep a per-row running top-k in shared memory
+//               and write k candidates per (row, column chunk); see topk_merge_kernel.
+// The x operand is a pre-shifted copy (x - b_dec, rounded to the MMA dtype) made by
+// shift_convert_kernel: a separate HBM pass costs <1% of the GEMM, whereas shifting in
+// shared memory would compete with the tensor cores for shared-memory bandwidth.
+#include <algorithm>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "sf_common.cuh"
+#include "sf_internal.h"
+
+namespace sf {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kThreads = 192;
+constexpr int kAccCols = 256;
+constexpr int kTmemCols = 512;
+constexpr int kTileABytes = kBM * 128;  // 128 rows x 128 B
+constexpr int kTileBBytes = kBN * 128;  // 256 rows (or MN chunks) x 128 B
+constexpr int kStageBytes = kTileABytes + kTileBBytes;
+
+enum Mode { kDense = 0, kTopk = 1 };
+
+struct TcParams {
+    int M, N, K;
+    int num_m_tiles, num_n_tiles;
+    int num_kb;
+    int group_m;          // dense: raster group height in m-tiles
+    int num_units;        // dense: tiles; topk: m_tiles * n_chunks
+    int n_chunks, tiles_per_chunk;
+    const void *b_enc;
+    int b_enc_dtype;
+    int64_t b_enc_stride;
+    const void *thr;
+    int thr_dtype;
+    int64_t thr_stride;
+    int activation;
+    void *out;
+    int out_dtype;
+    int64_t out_sm, out_sn;
+    int out_vec;
+    int32_t *row_nnz;
+    unsigned *err;
+    // topk
+    int k;
+    int values_dtype;
+    unsigned long long *cand;  // [M, n_chunks, k] packed keys
+};
+
+struct __align__(8) TcShared {
+    uint64_t full[8];
+    uint64_t empty[8];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort_flag;
+    float bias[2][kBN];
+    float thr[2][kBN];
+};
+
+// Unit u -> (m_blk, first n_blk, n-tile count).
+struct Unit {
+    int m_blk, n_first, n_count, chunk;
+};
+
+__device__ __forceinline__ Unit unit_coords(const TcParams &p, int u, int mode) {
+    Unit r;
+    if (mode == kDense) {
+        // Grouped raster: group_m m-tiles share each W n-tile while it is in L2.
+        const int per_group = p.group_m * p.num_n_tiles;
+        const int g = u / per_group;
+        const int first_m = g * p.group_m;
+        const int gm = min(p.num_m_tiles - first_m, p.group_m);
+        const int local = u - g * per_group;
+        r.m_blk = first_m + local % gm;
+        r.n_first = local / gm;
+        r.n_count = 1;
+        r.chunk = 0;
+    } else {
+        // Chunks of one m-tile run side by side so concurrent units share x tiles in L2.
+        r.chunk = u % p.n_chunks;
+        r.m_blk = u / p.n_chunks;
+        r.n_first = r.chunk * p.tiles_per_chunk;
+        r.n_count = min(p.tiles_per_chunk, p.num_n_tiles - r.n_first);
+    }
+    return r;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Bounded wait that ignores the abort flag: used only to drain copies in flight.
+__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity, unsigned *err) {
+    const uint32_t a = smem_u32(bar);
+    const unsigned long long t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(a, parity)) return;
+        if ((i & 31u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(err, kErrTimeout);
+            return;
+        }
+    }
+}
+
+template <typename OT>
+__device__ __forceinline__ void store_chunk(const TcParams &p, int row, int col0, const float (&v)[32],
+                                            uint64_t policy) {
+    OT *base = reinterpret_cast<OT *>(p.out) + (int64_t)row * p.out_sm;
+    if (p.out_vec && col0 + 32 <= p.N) {
+        constexpr int EPV = 16 / sizeof(OT);
+        OT *dst = base + col0;
+#pragma unroll
+        for (int j = 0; j < 32; j += EPV) {
+            uint4 pk;
+            OT *e = reinterpret_cast<OT *>(&pk);
+#pragma unroll
+            for (int t = 0; t < EPV; ++t) e[t] = from_f32<OT>(v[j + t]);
+            st_global_v4_hint(dst + j, pk, policy);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            if (col < p.N) base[(int64_t)col * p.out_sn] = from_f32<OT>(v[j]);
+        }
+    }
+}
+
+template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    encode_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const TcParams p) {
+    constexpr int ES = (AB_FMT == 2) ? 4 : 2;  // operand element bytes
+    constexpr int BK = 128 / ES;               // K elements per stage (one 128 B swizzle row)
+    constexpr int UMMA_K = 32 / ES;            // K per tcgen05.mma
+    constexpr int KSTEPS = BK / UMMA_K;        // 4
+    constexpr int MN_BOX = 128 / ES;           // MN-major B: elements per 128 B chunk
+    constexpr int MN_BOX_BYTES = BK * 128;     // one MN chunk: BK rows x 128 B
+    constexpr uint32_t IDESC = make_idesc(AB_FMT, B_MN, kBM, kBN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * kTileABytes;
+    TcShared *sh = reinterpret_cast<TcShared *>(smem + STAGES * kStageBytes);
+    unsigned long long *topk_lists = reinterpret_cast<unsigned long long *>(sh + 1);  // [k][128]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&sh->full[s], 1);
+            mbar_init(&sh->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sh->tmem_full[b], 1);
+            mbar_init(&sh->tmem_empty[b], 128);
+        }
+        mbar_init(&sh->drain, 1);
+        sh->abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(&sh->tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = sh->tmem_base;
+    volatile int *abort_flag = &sh->abort_flag;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            const uint64_t pol_x = l2_policy_evict_last();
+            const uint64_t pol_w = l2_policy_evict_normal();
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0;  // bit s: stage s armed at least once
+            uint32_t armed_parity = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                const Unit un = unit_coords(p, u, MODE);
+                for (int nt = 0; ok && nt < un.n_count; ++nt) {
+                    const int n_blk = un.n_first + nt;
+                    for (int kb = 0; kb < p.num_kb; ++kb) {
+                        if (!mbar_wait(&sh->empty[stage], phase ^ 1u, abort_flag, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&sh->full[stage], kStageBytes);
+                        armed |= 1u << stage;
+                        armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+                        uint8_t *a_dst = sA + stage * kTileABytes;
+                        uint8_t *b_dst = sB + stage * kTileBBytes;
+                        tma_load_2d(a_dst, &tmA, &sh->full[stage], kb * BK, un.m_blk * kBM, pol_x);
+                        if (B_MN) {
+#pragma unroll
+                            for (int j = 0; j < kBN / MN_BOX; ++j)
+                                tma_load_2d(b_dst + j * MN_BOX_BYTES, &tmB, &sh->full[stage],
+                                            n_blk * kBN + j * MN_BOX, kb * BK, pol_w);
+                        } else {
+                            tma_load_2d(b_dst, &tmB, &sh->full[stage], kb * BK, n_blk * kBN, pol_w);
+                        }
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // Let every copy this thread issued land before shared memory goes away.
+                for (int s = 0; s < STAGES; ++s)
+                    if (armed & (1u << s)) mbar_drain(&sh->full[s], (armed_parity >> s) & 1u, p.err);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                const Unit un = unit_coords(p, u, MODE);
+                for (int nt = 0; ok && nt < un.n_count; ++nt) {
+                    if (!mbar_wait(&sh->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + acc * kAccCols;
+                    for (int kb = 0; kb < p.num_kb; ++kb) {
+                        if (!mbar_wait(&sh->full[stage], phase, abort_flag, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(sA + stage * kTileABytes);
+                        const uint32_t b_addr = smem_u32(sB + stage * kTileBBytes);
+#pragma unroll
+                        for (int ks = 0; ks < KSTEPS; ++ks) {
+                            const uint64_t ad = smem_desc_sw128(a_addr + ks * 32, 16, 1024);
+                            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + ks * UMMA_K * 128, MN_BOX_BYTES, 1024)
+                                                     : smem_desc_sw128(b_addr + ks * 32, 16, 1024);
+                            const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
+                            if (AB_FMT == 2)
+                                umma_tf32(d_tmem, ad, bd, IDESC, accum);
+                            else
+                                umma_f16(d_tmem, ad, bd, IDESC, accum);
+                        }
+                        umma_commit(&sh->empty[stage]);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    umma_commit(&sh->tmem_full[acc]);
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                }
+            }
+            // Every MMA this thread issued has finished once `drain` completes.
+            umma_commit(&sh->drain);
+            mbar_drain(&sh->drain, 0, p.err);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int et = threadIdx.x - 64;  // 0..127
+        const int quad = warp & 3;        // TMEM lanes [32*quad, 32*quad+32)
+        const int row_in_tile = quad * 32 + lane;
+        const uint64_t pol_out = l2_policy_evict_first();
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        int tile_iter = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+            const Unit un = unit_coords(p, u, MODE);
+            const int row = un.m_blk * kBM + row_in_tile;
+            unsigned long long min_key = 0;
+            int min_slot = 0;
+            if (MODE == kTopk) {
+                for (int s = 0; s < p.k; ++s) topk_lists[s * 128 + et] = 0ull;
+            }
+            for (int nt = 0; nt < un.n_count; ++nt, ++tile_iter) {
+                const int n_blk = un.n_first + nt;
+                const int buf = tile_iter & 1;
+                // Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
+                for (int j = et; j < kBN; j += 128) {
+                    const int col = n_blk * kBN + j;
+                    float b = 0.f, t = 0.f;
+                    if (col < p.N) {
+                        b = load_as_f32(p.b_enc, p.b_enc_dtype, (int64_t)col * p.b_enc_stride);
+                        if (MODE == kDense && p.activation == SF_ACT_JUMPRELU)
+                            t = load_as_f32(p.thr, p.thr_dtype, (int64_t)col * p.thr_stride);
+                    }
+                    sh->bias[buf][j] = b;
+                    sh->thr[buf][j] = t;
+                }
+                named_bar_sync(1, 128);
+
+                if (!mbar_wait(&sh->tmem_full[acc], acc_phase, abort_flag, p.err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
+                int cnt = 0;
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c * 32, r);
+                    tmem_ld_wait();
+                    if (c == kBN / 32 - 1) {
+                        tc_fence_before();
+                        mbar_arrive(&sh->tmem_empty[acc]);
+                    }
+                    const int col0 = n_blk * kBN + c * 32;
+                    if (MODE == kDense) {
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
+                            float o = fmaxf(pre, 0.f);
+                            if (p.activation == SF_ACT_JUMPRELU) o = (pre > sh->thr[buf][c * 32 + j]) ? o : 0.f;
+                            o = round_to(o, p.out_dtype);
+                            v[j] = o;
+                            cnt += (o != 0.f && col0 + j < p.N) ? 1 : 0;
+                        }
+                        if (row < p.M) {
+                            if (p.out_dtype == SF_BF16)
+                                store_chunk<__nv_bfloat16>(p, row, col0, v, pol_out);
+                            else if (p.out_dtype == SF_F16)
+                                store_chunk<__half>(p, row, col0, v, pol_out);
+                            else
+                                store_chunk<float>(p, row, col0, v, pol_out);
+                        }
+                    } else {
+#pragma unroll 4
+                        for (int j = 0; j < 32; ++j) {
+                            const int col = col0 + j;
+                            if (col >= p.N) break;
+                            const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
+                            const float o = round_to(fmaxf(pre, 0.f), p.values_dtype);
+                            const unsigned long long key =
+                                (static_cast<unsigned long long>(__float_as_uint(o) & 0x7FFFFFFFu) << 32) |
+                                static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
+                            if (key > min_key) {
+                                topk_lists[min_slot * 128 + et] = key;
+                                min_key = ~0ull;
+                                for (int s = 0; s < p.k; ++s) {
+                                    const unsigned long long q = topk_lists[s * 128 + et];
+                                    if (q < min_key) {
+                                        min_key = q;
+                                        min_slot = s;
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+                if (MODE == kDense && p.row_nnz != nullptr && row < p.M && cnt != 0) atomicAdd(p.row_nnz + row, cnt);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (MODE == kTopk && ok && row < p.M) {
+                unsigned long long *dst = p.cand + ((int64_t)row * p.n_chunks + un.chunk) * p.k;
+                for (int s = 0; s < p.k; ++s) dst[s] = topk_lists[s * 128 + et];
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// -------------------------------------------------------------------------------------
+// Tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point).
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+int make_map_2d(CUtensorMap *map, const void *base, int ab_fmt, uint64_t inner, uint64_t outer,
+                uint64_t row_pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+    auto fn = get_encode_tiled();
+    if (!fn) return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const CUtensorMapDataType dt = ab_fmt == 2   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : ab_fmt == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_pitch_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(SF_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) inner=%llu outer=%llu pitch=%llu", (int)r,
+                         (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)row_pitch_bytes);
+    return SF_OK;
+}
+
+template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+int launch_typed(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
+                 cudaStream_t stream) {
+    auto kern = encode_tc_kernel<AB_FMT, B_MN, MODE, STAGES>;
+    const size_t smem = 1024 + (size_t)STAGES * kStageBytes + sizeof(TcShared) + extra_smem;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(encode_tc)");
+    const int grid = std::max(1, std::min(p.num_units, num_sms()));
+    kern<<<grid, kThreads, smem, stream>>>(tmA, tmB, p);
+    return check_cuda(cudaGetLastError(), "encode_tc launch");
+}
+
+template <int MODE, int STAGES>
+int dispatch(int ab_fmt, bool b_mn, const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
+             size_t extra_smem, cudaStream_t s) {
+    if (ab_fmt == 1) return b_mn ? launch_typed<1, true, MODE, STAGES>(tmA, tmB, p, extra_smem, s)
+                                 : launch_typed<1, false, MODE, STAGES>(tmA, tmB, p, extra_smem, s);
+    if (ab_fmt == 0) return b_mn ? launch_typed<0, true, MODE, STAGES>(tmA, tmB, p, extra_smem, s)
+                                 : launch_typed<0, false, MODE, STAGES>(tmA, tmB, p, extra_smem, s);
+    return b_mn ? launch_typed<2, true, MODE, STAGES>(tmA, tmB, p, extra_smem, s)
+                : launch_typed<2, false, MODE, STAGES>(tmA, tmB, p, extra_smem, s);
+}
+
+int build_maps(const GemmOperands &g, CUtensorMap *tmA, CUtensorMap *tmB) {
+    const int es = g.ab_fmt == 2 ? 4 : 2;
+    const uint32_t bk = 128 / es;
+    int st = make_map_2d(tmA, g.a, g.ab_fmt, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.a_pitch * es, bk, kBM);
+    if (st) return st;
+    if (g.b_mn_major)  // W[k, n] at b + k*b_pitch + n
+        return make_map_2d(tmB, g.b, g.ab_fmt, (uint64_t)g.N, (uint64_t)g.K, (uint64_t)g.b_pitch * es, 128 / es, bk);
+    // W[k, n] at b + n*b_pitch + k
+    return make_map_2d(tmB, g.b, g.ab_fmt, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.b_pitch * es, bk, kBN);
+}
+
+void fill_common(TcParams &p, const GemmOperands &g, unsigned *err) {
+    const int es = g.ab_fmt == 2 ? 4 : 2;
+    p.M = (int)g.M;
+    p.N = (int)g.N;
+    p.K = (int)g.K;
+    p.num_m_tiles = (int)((g.M + kBM - 1) / kBM);
+    p.num_n_tiles = (int)((g.N + kBN - 1) / kBN);
+    p.num_kb = (int)((g.K + (128 / es) - 1) / (128 / es));
+    p.err = err;
+}
+
+}  // namespace
+
+int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, cudaStream_t stream) {
+    CUtensorMap tmA, tmB;
+    int st = build_maps(g, &tmA, &tmB);
+    if (st) return st;
+    TcParams p{};
+    fill_common(p, g, device_error_word());
+    // x (A) stays L2-resident when a group of m-tiles fits in ~64 MB.
+    const int es = g.ab_fmt == 2 ? 4 : 2;
+    const int64_t a_tile_bytes = (int64_t)kBM * g.K * es;
+    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, (64ll << 20) / std::max<int64_t>(1, a_tile_bytes)));
+    p.num_units = p.num_m_tiles * p.num_n_tiles;
+    p.n_chunks = 1;
+    p.tiles_per_chunk = 1;
+    p.b_enc = ep.b_enc;
+    p.b_enc_dtype = ep.b_enc_dtype;
+    p.b_enc_stride = ep.b_enc_stride;
+    p.thr = ep.thr;
+    p.thr_dtype = ep.thr_dtype;
+    p.thr_stride = ep.thr_stride;
+    p.activation = ep.activation;
+    p.out = ep.out;
+    p.out_dtype = ep.out_dtype;
+    p.out_sm = ep.out_sm;
+    p.out_sn = ep.out_sn;
+    p.out_vec = ep.out_vec;
+    p.row_nnz = ep.row_nnz;
+    return dispatch<kDense, 4>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
+}
+
+// Column chunks per row for the top-k schedule: enough (m-tile, chunk) units to fill the
+// SMs in whole waves.
+int topk_chunks(int64_t M, int64_t N) {
+    const int m_tiles = (int)((M + kBM - 1) / kBM);
+    const int n_tiles = (int)((N + kBN - 1) / kBN);
+    const int sms = num_sms();
+    int best = 1;
+    double best_eff = -1.0;
+    for (int c = 1; c <= std::min(n_tiles, 32); ++c) {
+        const int tpc = (n_tiles + c - 1) / c;
+        const int chunks = (n_tiles + tpc - 1) / tpc;
+        const long units = (long)m_tiles * chunks;
+        const long waves = (units + sms - 1) / sms;
+        double eff = (double)units / (double)(waves * sms);
+        eff -= 0.002 * c;  // prefer fewer candidates at equal balance
+        if (eff > best_eff + 1e-9) {
+            best_eff = eff;
+            best = chunks;
+        }
+    }
+    return best;
+}
+
+int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t stream) {
+    CUtensorMap tmA, tmB;
+    int st = build_maps(g, &tmA, &tmB);
+    if (st) return st;
+    TcParams p{};
+    fill_common(p, g, device_error_word());
+    p.group_m = 1;
+    const int chunks = tk.n_chunks;
+    p.tiles_per_chunk = (p.num_n_tiles + chunks - 1) / chunks;
+    p.n_chunks = (p.num_n_tiles + p.tiles_per_chunk - 1) / p.tiles_per_chunk;
+    if (p.n_chunks != chunks) return set_error(SF_ERR_INVALID, "top-k chunk count %d is not realisable", chunks);
+    p.num_units = p.num_m_tiles * p.n_chunks;
+    p.b_enc = tk.b_enc;
+    p.b_enc_dtype = tk.b_enc_dtype;
+    p.b_enc_stride = tk.b_enc_stride;
+    p.activation = SF_ACT_RELU;
+    p.k = tk.k;
+    p.values_dtype = tk.values_dtype;
+    p.cand = tk.cand;
+    if (tk.k < 1 || tk.k > kTopkMaxK) return set_error(SF_ERR_UNSUPPORTED, "fused top-k supports 1 <= k <= %d", kTopkMaxK);
+    const size_t lists = (size_t)tk.k * 128 * sizeof(unsigned long long);
+    if (tk.k <= 64) return dispatch<kTopk, 3>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+    return dispatch<kTopk, 2>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+}
+
+}  // namespace sf

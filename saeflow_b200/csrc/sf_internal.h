@@ -1,0 +1,57 @@
+// Host-side interfaces between the saeflow_b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sf {
+
+// GEMM operands as the tensor-core kernel reads them through TMA.
+//   A: [M, K] K-contiguous, row pitch a_pitch elements (16-byte multiple), MMA dtype.
+//   B: W_enc as [K, N]; b_mn_major: element (k, n) at b[k*b_pitch + n] (N-contiguous),
+//      else at b[n*b_pitch + k] (K-contiguous).
+struct GemmOperands {
+    const void *a;
+    int64_t a_pitch;
+    const void *b;
+    int64_t b_pitch;
+    bool b_mn_major;
+    int ab_fmt;  // 0 fp16, 1 bf16, 2 tf32 (fp32 storage)
+    int64_t M, N, K;
+};
+
+struct EpilogueArgs {
+    const void *b_enc;
+    int b_enc_dtype;
+    int64_t b_enc_stride;
+    const void *thr;
+    int thr_dtype;
+    int64_t thr_stride;
+    int activation;
+    void *out;
+    int out_dtype;
+    int64_t out_sm, out_sn;
+    int out_vec;
+    int32_t *row_nnz;
+};
+
+struct TopkArgs {
+    const void *b_enc;
+    int b_enc_dtype;
+    int64_t b_enc_stride;
+    int k;
+    int values_dtype;
+    int n_chunks;
+    unsigned long long *cand;  // [M, n_chunks, k]
+};
+
+int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, cudaStream_t stream);
+int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t stream);
+int topk_chunks(int64_t M, int64_t N);
+constexpr int kTopkMaxK = 120;  // shared-memory bound of the fused top-k lists
+
+int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
+                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream);
+
+}  // namespace sf
