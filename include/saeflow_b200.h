@@ -148,6 +148,27 @@ SF_API int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *ind
                      const sf_matrix *out, sf_stream stream);
 
 /*
+ * sf_fused_encode without a caller-supplied workspace, for callers that cannot allocate
+ * device memory: a foreign-language host handed only input/output buffers by the
+ * framework that owns the GPU, a process whose caching allocator already holds nearly
+ * all device memory, or a loop that cannot take cudaMalloc's implicit synchronisation.
+ * It has no counterpart in the reference (whose Triton launch needs no workspace).
+ *
+ * The workspace is a 16 MiB array in the library's device image (held by every GPU that
+ * loads the library's device code, until exit); this call allocates nothing. Operands
+ * whose sf_fused_encode_workspace exceeds 16 MiB are rejected with SF_ERR_WORKSPACE
+ * (e.g. bf16 x with d_in=2304: at most 3640 rows per call). The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture. Every call on a device shares the one array: calls whose kernels
+ * overlap on the GPU (other streams, other host threads) race on it; serialise them.
+ * Arguments and results are those of sf_fused_encode.
+ */
+SF_API int sf_fused_encode_noalloc(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
+                                   const sf_vector *b_dec, const sf_vector *threshold, int activation,
+                                   const sf_matrix *out, int32_t *row_nnz, int allow_tf32, int variant,
+                                   sf_stream stream);
+
+/*
  * Workspace bytes for sf_topk_encode.
  */
 SF_API int sf_topk_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int k, int allow_tf32,

@@ -51,6 +51,7 @@ SIGNATURES = {
     "sf_fused_encode_workspace": (_c.c_int, [_MP, _MP, _c.c_int, _c.c_int, _SIZE_P]),
     "sf_fused_encode": (_c.c_int, [_MP, _MP, _VP, _VP, _VP, _c.c_int, _MP, _P, _c.c_int, _c.c_int,
                                    _P, _c.c_size_t, _P]),
+    "sf_fused_encode_noalloc": (_c.c_int, [_MP, _MP, _VP, _VP, _VP, _c.c_int, _MP, _P, _c.c_int, _c.c_int, _P]),
     "sf_row_nnz": (_c.c_int, [_MP, _P, _P]),
     "sf_csr_indptr": (_c.c_int, [_P, _c.c_int64, _P, _P]),
     "sf_dense_to_csr": (_c.c_int, [_MP, _P, _P, _P, _c.c_int, _P]),

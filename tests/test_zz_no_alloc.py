@@ -1,0 +1,91 @@
+"""sf_fused_encode_noalloc, the encode entry point that allocates nothing, against the
+allocating sf_fused_encode (B200).
+
+The no-alloc entry point serves callers that cannot allocate device memory (a
+foreign-language host given only its input and output buffers, a process whose caching
+allocator holds the GPU's memory, a loop that cannot take cudaMalloc's synchronisation):
+its workspace is a fixed 16 MiB array in the library's device image. This file is
+collected last so that a run stopping at the first failure has run every other test.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from saeflow_b200 import _abi
+
+pytestmark = pytest.mark.gpu
+
+SCRATCH_BYTES = 16 << 20
+RTOL = 3e-2  # bf16 tolerance of the kernel tests
+
+
+def _operands(M, K, N, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    W_dec = torch.randn(N, K, generator=g, device="cuda")
+    W_dec /= W_dec.norm(dim=1, keepdim=True)
+    W = W_dec.T.contiguous().to(torch.bfloat16)
+    b_enc = (torch.randn(N, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    b_dec = (torch.randn(K, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    thr = (torch.rand(N, generator=g, device="cuda") * 0.3).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    return x, W, b_enc, b_dec, thr
+
+
+def _structs(x, W, b_enc, b_dec, thr, out):
+    return (_abi.matrix(x, "x"), _abi.matrix(W, "W_enc"), _abi.vector(b_enc, "b_enc"), _abi.vector(b_dec, "b_dec"),
+            _abi.vector(thr, "threshold"), _abi.matrix(out, "out"))
+
+
+def _encode_allocating(lib, x, W, b_enc, b_dec, thr):
+    out = torch.empty(x.shape[0], W.shape[1], device="cuda", dtype=torch.bfloat16)
+    nnz = torch.zeros(x.shape[0], device="cuda", dtype=torch.int32)
+    xm, wm, be, bd, th, om = _structs(x, W, b_enc, b_dec, thr, out)
+    need = ctypes.c_size_t(0)
+    _abi.check(lib.sf_fused_encode_workspace(ctypes.byref(xm), ctypes.byref(wm), 0, 0, ctypes.byref(need)))
+    ws = torch.empty(need.value, device="cuda", dtype=torch.uint8)
+    _abi.check(lib.sf_fused_encode(ctypes.byref(xm), ctypes.byref(wm), ctypes.byref(be), ctypes.byref(bd),
+                                   ctypes.byref(th), _abi.SF_ACT_JUMPRELU, ctypes.byref(om), nnz.data_ptr(), 0, 0,
+                                   ws.data_ptr(), ws.numel(), _abi.stream_of(x.device)))
+    return out, nnz, need.value
+
+
+def _encode_noalloc(lib, x, W, b_enc, b_dec, thr, out, nnz):
+    xm, wm, be, bd, th, om = _structs(x, W, b_enc, b_dec, thr, out)
+    return lib.sf_fused_encode_noalloc(ctypes.byref(xm), ctypes.byref(wm), ctypes.byref(be), ctypes.byref(bd),
+                                       ctypes.byref(th), _abi.SF_ACT_JUMPRELU, ctypes.byref(om), nnz.data_ptr(), 0,
+                                       0, _abi.stream_of(x.device))
+
+
+def test_noalloc_encode_matches_allocating_encode_on_two_calls():
+    lib = _abi.load()
+    K, N = 512, 4096
+    # two calls in a row, different inputs and row counts: the second must not see the
+    # first call's scratch contents
+    for M, seed in ((1000, 11), (3000, 12)):
+        x, W, b_enc, b_dec, thr = _operands(M, K, N, seed)
+        want, want_nnz, need = _encode_allocating(lib, x, W, b_enc, b_dec, thr)
+        assert need <= SCRATCH_BYTES
+        got = torch.full_like(want, float("nan"))
+        nnz = torch.zeros(M, device="cuda", dtype=torch.int32)
+        _abi.check(_encode_noalloc(lib, x, W, b_enc, b_dec, thr, got, nnz))
+        torch.cuda.synchronize()
+        torch.testing.assert_close(got.float(), want.float(), atol=RTOL, rtol=RTOL)
+        assert torch.equal(nnz, want_nnz)
+        assert torch.equal(nnz.cpu(), torch.count_nonzero(got, dim=1).int().cpu())
+    assert _abi.device_error() == 0
+
+
+def test_noalloc_encode_rejects_operands_beyond_its_scratch():
+    lib = _abi.load()
+    K, N = 2304, 512
+    M = SCRATCH_BYTES // (K * 2) + 1  # one row more than the scratch holds
+    x, W, b_enc, b_dec, thr = _operands(M, K, N, 13)
+    out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
+    nnz = torch.zeros(M, device="cuda", dtype=torch.int32)
+    st = _encode_noalloc(lib, x, W, b_enc, b_dec, thr, out, nnz)
+    assert st == _abi.SF_ERR_WORKSPACE
+    assert b"scratch" in lib.sf_last_error()
+    torch.cuda.synchronize()
+    assert int(nnz.abs().sum()) == 0 and int(out.float().abs().sum()) == 0  # nothing ran
