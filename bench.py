@@ -22,7 +22,6 @@ import argparse
 import json
 import math
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -156,65 +155,63 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples of this GPU's SM clock and throttle reasons during the timed region."""
+    """SM clock and throttle reasons of this GPU, sampled every 10 ms through NVML while
+    the timed region runs (nvidia-smi's 200 ms loop misses short regions)."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap,utilization.gpu")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index):
-        self.proc = None
-        self.lines = []
+    def __init__(self, device_index, period_s=0.01):
+        self.samples = []
+        self.period = period_s
+        self.stop = threading.Event()
+        self.handle = None
         try:
+            import pynvml
+
+            pynvml.nvmlInit()
             uuid = str(torch.cuda.get_device_properties(device_index).uuid)
-            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
-        except Exception:  # noqa: BLE001
-            ident = str(device_index)
-        self.cmd = ["nvidia-smi", f"--id={ident}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                    "-lms", "200"]
+            uuid = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.nv = pynvml
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode() if isinstance(uuid, str) else uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - no NVML: report no samples
+            self.handle = None
+
+    def _run(self):
+        nv = self.nv
+        while not self.stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                util = nv.nvmlDeviceGetUtilizationRates(self.handle).gpu
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((sm, util, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            self.stop.wait(self.period)
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+        if self.handle is not None:
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except (OSError, ValueError):
-            self.proc = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self.handle is not None:
+            self.stop.set()
             self.thread.join(timeout=2)
 
     def summary(self):
-        rows = []
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                rows.append(dict(sm=float(parts[0]), max=float(parts[1]), util=float(parts[7]),
-                                 reasons=[n for n, v in zip(("hw_slowdown", "hw_thermal_slowdown",
-                                                             "sw_thermal_slowdown", "sw_power_cap"), parts[3:7])
-                                          if v.lower().startswith("active")]))
-            except ValueError:
-                continue
-        if not rows:
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        loaded = [r for r in rows if r["util"] >= 50] or rows
-        sms = sorted(r["sm"] for r in loaded)
-        reasons = sorted({x for r in loaded for x in r["reasons"]})
-        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": max(r["max"] for r in rows), "reasons": reasons,
-                "samples": len(rows), "samples_under_load": len(loaded)}
+        loaded = [s for s in self.samples if s[1] >= 50] or self.samples
+        sms = sorted(s[0] for s in loaded)
+        seen = 0
+        for s in loaded:
+            seen |= s[2]
+        reasons = sorted(n for n, bit in self.REASONS.items() if seen & bit)
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "samples_under_load": len(loaded), "source": "nvml 10 ms"}
 
 
 def l2_flush(buf):

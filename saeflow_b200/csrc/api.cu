@@ -20,6 +20,7 @@ int launch_decode(const int64_t *indptr, int64_t M, const int32_t *indices, cons
                   const sf_matrix &W, const sf_vector *b, const sf_matrix &out, cudaStream_t s);
 int launch_topk_merge(const unsigned long long *cand, int64_t M, int ncand, int k, int32_t *out_idx, void *out_val,
                       int vdt, cudaStream_t s);
+int launch_topk_rows(const sf_matrix &f, int k, int32_t *out_idx, void *out_val, int vdt, cudaStream_t s);
 
 namespace {
 thread_local char g_last_error[512] = "";
@@ -527,20 +528,68 @@ int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *indices, c
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+namespace sf {
+namespace {
+
+constexpr int kTopkDenseMaxK = 200;         // shared-memory bound of topk_rows_kernel
+constexpr int64_t kTopkDenseChunk = 256ll << 20;  // bytes of dense features per row chunk
+
+// The fused epilogue selects on tensor-core products: 16-bit operands, or fp32 with TF32
+// allowed (or non-fp32 x, the reference's own rule, encode.py:118-120). fp32 with IEEE
+// products, and k beyond the epilogue's limit, take the dense route: encode a chunk of
+// rows (CUDA-core kernel for IEEE fp32), then select per row from the stored values.
+bool topk_fused(const sf_matrix *x, const sf_matrix *W, int k, int allow_tf32) {
+    if (k > kTopkMaxK) return false;
+    if (W->dtype != SF_F32) return true;
+    return allow_tf32 || x->dtype != SF_F32;
+}
+
+int64_t topk_chunk_rows(const sf_matrix *x, const sf_matrix *W) {
+    const int64_t per_row = W->cols * (int64_t)dtype_size(x->dtype);
+    int64_t r = kTopkDenseChunk / (per_row > 0 ? per_row : 1);
+    if (r < 1) r = 1;
+    return r < x->rows ? r : x->rows;
+}
+
+int topk_workspace(const sf_matrix *x, const sf_matrix *W, int k, int allow_tf32, size_t *bytes) {
+    if (topk_fused(x, W, k, allow_tf32)) {
+        EncodePlan pl;
+        int st = plan_encode(x, W, 1, SF_VARIANT_TCGEN05, &pl);
+        if (st) return st;
+        const int chunks = topk_chunks(x->rows, W->cols);
+        *bytes = (size_t)round_up((int64_t)plan_workspace(pl), 256) +
+                 (size_t)x->rows * chunks * k * sizeof(unsigned long long);
+        return SF_OK;
+    }
+    if (k > kTopkDenseMaxK) return set_error(SF_ERR_UNSUPPORTED, "top-k supports k <= %d", kTopkDenseMaxK);
+    sf_matrix xr = *x;
+    xr.rows = topk_chunk_rows(x, W);
+    size_t enc = 0;
+    int st = sf_fused_encode_workspace(&xr, W, allow_tf32, SF_VARIANT_AUTO, &enc);
+    if (st) return st;
+    *bytes = (size_t)round_up((int64_t)enc, 256) + (size_t)xr.rows * W->cols * dtype_size(x->dtype);
+    return SF_OK;
+}
+
+}  // namespace
+}  // namespace sf
+
+extern "C" {
+
 int sf_topk_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int k, int allow_tf32, size_t *bytes) {
     if (!bytes) return set_error(SF_ERR_INVALID, "bytes is NULL");
     *bytes = 0;
     int st = check_matrix(x, "x");
     if (!st) st = check_matrix(W_enc, "W_enc");
     if (st) return st;
-    if (k < 1 || k > W_enc->cols) return set_error(SF_ERR_INVALID, "k=%d must be in [1, d_sae=%lld]", k, (long long)W_enc->cols);
-    EncodePlan pl;
-    st = plan_encode(x, W_enc, 1, SF_VARIANT_TCGEN05, &pl);
-    if (st) return st;
-    (void)allow_tf32;
-    const int chunks = topk_chunks(x->rows, W_enc->cols);
-    *bytes = plan_workspace(pl) + 256 + (size_t)x->rows * chunks * k * sizeof(unsigned long long);
-    return SF_OK;
+    if (x->cols != W_enc->rows)
+        return set_error(SF_ERR_INVALID, "x has d_in=%lld but W_enc has d_in=%lld", (long long)x->cols,
+                         (long long)W_enc->rows);
+    if (k < 1 || k > W_enc->cols)
+        return set_error(SF_ERR_INVALID, "k=%d must be in [1, d_sae=%lld]", k, (long long)W_enc->cols);
+    return topk_workspace(x, W_enc, k, allow_tf32, bytes);
 }
 
 int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc, const sf_vector *b_dec, int k,
@@ -554,27 +603,52 @@ int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *
         return set_error(SF_ERR_INVALID, "x has d_in=%lld but W_enc has d_in=%lld", (long long)K,
                          (long long)W_enc->rows);
     if (k < 1 || k > N) return set_error(SF_ERR_INVALID, "k=%d must be in [1, d_sae=%lld]", k, (long long)N);
-    if (k > kTopkMaxK) return set_error(SF_ERR_UNSUPPORTED, "fused top-k supports k <= %d", kTopkMaxK);
     if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
     st = check_vector(b_enc, N, "b_enc", false);
     if (!st) st = check_vector(b_dec, K, "b_dec", true);
     if (st) return st;
     if (M == 0) return SF_OK;
     if (!indices || !values) return set_error(SF_ERR_INVALID, "indices/values are NULL");
-    (void)allow_tf32;  // fp32 W_enc always runs this path on TF32 tensor cores
-
-    EncodePlan pl;
-    st = plan_encode(x, W_enc, 1, SF_VARIANT_TCGEN05, &pl);
+    size_t need = 0;
+    st = topk_workspace(x, W_enc, k, allow_tf32, &need);
     if (st) return st;
-    const int chunks = topk_chunks(M, N);
-    const size_t base = plan_workspace(pl);
-    const size_t cand_off = (size_t)round_up((int64_t)base, 256);
-    const size_t need = cand_off + (size_t)M * chunks * k * sizeof(unsigned long long);
     if (workspace_bytes < need || !workspace)
         return set_error(SF_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
     if (!aligned16(workspace)) return set_error(SF_ERR_WORKSPACE, "workspace must be 16-byte aligned");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
+
+    if (!topk_fused(x, W_enc, k, allow_tf32)) {
+        // Dense route: the stored ReLU output (in the values dtype, as the reference's
+        // fused_encode(..., "relu") stores it in x's dtype) is selected row by row.
+        const int64_t R = topk_chunk_rows(x, W_enc);
+        sf_matrix xr = *x;
+        xr.rows = R;
+        size_t enc = 0;
+        st = sf_fused_encode_workspace(&xr, W_enc, allow_tf32, SF_VARIANT_AUTO, &enc);
+        if (st) return st;
+        uint8_t *fbuf = ws + round_up((int64_t)enc, 256);
+        const size_t xes = dtype_size(x->dtype), ves = dtype_size(values_dtype);
+        for (int64_t r0 = 0; r0 < M; r0 += R) {
+            const int64_t rr = (M - r0) < R ? (M - r0) : R;
+            xr.data = static_cast<const uint8_t *>(x->data) + r0 * x->stride_row * (int64_t)xes;
+            xr.rows = rr;
+            sf_matrix fr{fbuf, values_dtype, 0, rr, N, N, 1};
+            st = sf_fused_encode(&xr, W_enc, b_enc, b_dec, nullptr, SF_ACT_RELU, &fr, nullptr, allow_tf32,
+                                 SF_VARIANT_AUTO, ws, enc, stream);
+            if (st) return st;
+            st = launch_topk_rows(fr, k, indices + r0 * k, static_cast<uint8_t *>(values) + r0 * k * (int64_t)ves,
+                                  values_dtype, s);
+            if (st) return st;
+        }
+        return SF_OK;
+    }
+
+    EncodePlan pl;
+    st = plan_encode(x, W_enc, 1, SF_VARIANT_TCGEN05, &pl);
+    if (st) return st;
+    const int chunks = topk_chunks(M, N);
+    const size_t cand_off = (size_t)round_up((int64_t)plan_workspace(pl), 256);
     void *xs = ws;
     void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
     auto *cand = reinterpret_cast<unsigned long long *>(ws + cand_off);

@@ -435,6 +435,73 @@ __global__ void __launch_bounds__(128) topk_merge_kernel(const unsigned long lon
     }
 }
 
+// ------------------------------------------------------------------ dense-row top-k
+// One CTA of 128 threads per row of a dense ReLU output f (values >= 0): each thread keeps
+// the k largest packed (value, ~column) keys of its columns in shared memory, sorts them,
+// and k rounds of a block-wide max emit the row's top-k sorted by value descending, ties
+// by lower column. Used for fp32 IEEE TopK and for k beyond the fused epilogue's limit.
+template <typename T, typename VT>
+__global__ void __launch_bounds__(128) topk_rows_kernel(const T *__restrict__ f, int64_t N, int64_t ld, int k,
+                                                        int32_t *__restrict__ out_idx, VT *__restrict__ out_val) {
+    extern __shared__ unsigned long long lists[];  // [k][128]
+    __shared__ unsigned long long warp_best[4];
+    __shared__ unsigned long long winner;
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    const int64_t row = blockIdx.x;
+    const T *rp = f + row * ld;
+    for (int s = 0; s < k; ++s) lists[s * 128 + t] = 0ull;
+    unsigned long long min_key = 0;
+    int min_slot = 0;
+    for (int64_t c = t; c < N; c += 128) {
+        const uint32_t bits = __float_as_uint(to_f32(rp[c])) & 0x7FFFFFFFu;
+        const unsigned long long key =
+            (static_cast<unsigned long long>(bits) << 32) | (0xFFFFFFFFull - static_cast<unsigned long long>(c));
+        if (key > min_key) {
+            lists[min_slot * 128 + t] = key;
+            min_key = ~0ull;
+            for (int s = 0; s < k; ++s) {
+                const unsigned long long q = lists[s * 128 + t];
+                if (q < min_key) {
+                    min_key = q;
+                    min_slot = s;
+                }
+            }
+        }
+    }
+    // sort this thread's list descending (insertion sort, k <= a few hundred)
+    for (int i = 1; i < k; ++i) {
+        const unsigned long long v = lists[i * 128 + t];
+        int j = i - 1;
+        while (j >= 0 && lists[j * 128 + t] < v) {
+            lists[(j + 1) * 128 + t] = lists[j * 128 + t];
+            --j;
+        }
+        lists[(j + 1) * 128 + t] = v;
+    }
+    int head = 0;
+    for (int r = 0; r < k; ++r) {
+        unsigned long long mine = head < k ? lists[head * 128 + t] : 0ull;
+        unsigned long long best = mine;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+            best = o > best ? o : best;
+        }
+        if (lane == 0) warp_best[w] = best;
+        __syncthreads();
+        if (t == 0) {
+            unsigned long long b = warp_best[0];
+            for (int i = 1; i < 4; ++i) b = warp_best[i] > b ? warp_best[i] : b;
+            winner = b;
+            const uint32_t col = 0xFFFFFFFFu - static_cast<uint32_t>(b & 0xFFFFFFFFull);
+            out_idx[row * k + r] = (int32_t)col;
+            out_val[row * k + r] = from_f32<VT>(__uint_as_float(static_cast<uint32_t>(b >> 32)));
+        }
+        __syncthreads();
+        if (head < k && mine == winner && mine != 0ull) ++head;
+    }
+}
+
 template <typename F>
 int by_dtype(int dt, F &&f) {
     if (dt == SF_F32) return f(float{});
@@ -568,4 +635,23 @@ int launch_topk_merge(const unsigned long long *cand, int64_t M, int ncand, int 
     });
 }
 
+}  // namespace sf
+
+namespace sf {
+int launch_topk_rows(const sf_matrix &f, int k, int32_t *out_idx, void *out_val, int vdt, cudaStream_t s) {
+    if (f.rows == 0) return SF_OK;
+    const size_t smem = (size_t)k * 128 * sizeof(unsigned long long);
+    return by_dtype(f.dtype, [&](auto tag) {
+        using T = decltype(tag);
+        return by_dtype(vdt, [&](auto vtag) {
+            using VT = decltype(vtag);
+            auto kern = topk_rows_kernel<T, VT>;
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(topk_rows)");
+            kern<<<(unsigned)f.rows, 128, smem, s>>>(reinterpret_cast<const T *>(f.data), f.cols, f.stride_row, k,
+                                                     out_idx, reinterpret_cast<VT *>(out_val));
+            return check_cuda(cudaGetLastError(), "topk rows launch");
+        });
+    });
+}
 }  // namespace sf

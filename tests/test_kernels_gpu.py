@@ -286,6 +286,24 @@ def test_topk_encode_vs_oracle(dtype, shape, k):
     assert_topk_matches(vals, idx, x, sae.W_enc, sae.b_enc, sae.b_dec, k)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_topk_encode_large_k_dense_route(dtype):
+    """k above the fused epilogue's limit: encode densely, then select per row."""
+    M, d_in, d_sae, k = 50, 64, 900, 150
+    sae = make_sae(d_in, d_sae, "topk", dtype, k=k).to("cuda")
+    x = torch.randn(M, d_in, device="cuda").to(dtype)
+    vals, idx = topk_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, k)
+    assert_topk_matches(vals, idx, x, sae.W_enc, sae.b_enc, sae.b_dec, k)
+
+
+def test_topk_encode_fp32_tf32_allowed():
+    """fp32 with TF32 allowed takes the fused tensor-core route (the reference's tf32 rule)."""
+    sae = make_sae(128, 2000, "topk", torch.float32, k=32).to("cuda")
+    x = torch.randn(300, 128, device="cuda")
+    vals, idx = topk_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, 32, allow_tf32=True)
+    assert_topk_matches(vals, idx, x, sae.W_enc, sae.b_enc, sae.b_dec, 32)
+
+
 # ----------------------------------------------------------------------------- ops
 
 @pytest.mark.parametrize("activation", ["relu", "jumprelu", "topk"])
