@@ -56,8 +56,9 @@ enum sf_status {
 /* Encode variant selector (the `config=` kwarg of fused_encode).                  */
 enum sf_encode_variant {
     SF_VARIANT_AUTO = 0,     /* tensor cores for 16-bit / TF32, CUDA cores for IEEE fp32 */
-    SF_VARIANT_TCGEN05 = 1,  /* force the tcgen05/TMEM kernel                        */
-    SF_VARIANT_SIMT = 2      /* force the CUDA-core kernel                           */
+    SF_VARIANT_TCGEN05 = 1,  /* force the tcgen05/TMEM kernel (CTA pairs when M > 128) */
+    SF_VARIANT_SIMT = 2,     /* force the CUDA-core kernel                           */
+    SF_VARIANT_TCGEN05_SINGLE = 3  /* tcgen05 kernel on single CTAs (128 x 256 tiles)  */
 };
 
 /* A strided 2-D tensor: element (i, j) is at data + (i*stride_row + j*stride_col)*size. */

@@ -19,7 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libsaeflow_b200.so"
 SF_F32, SF_BF16, SF_F16 = 0, 1, 2
 DTYPE_CODES = {torch.float32: SF_F32, torch.bfloat16: SF_BF16, torch.float16: SF_F16}
 SF_ACT_RELU, SF_ACT_JUMPRELU = 0, 1
-SF_VARIANT_AUTO, SF_VARIANT_TCGEN05, SF_VARIANT_SIMT = 0, 1, 2
+SF_VARIANT_AUTO, SF_VARIANT_TCGEN05, SF_VARIANT_SIMT, SF_VARIANT_TCGEN05_SINGLE = 0, 1, 2, 3
 
 SF_OK, SF_ERR_INVALID, SF_ERR_UNSUPPORTED, SF_ERR_CUDA, SF_ERR_WORKSPACE, SF_ERR_DEVICE = range(6)
 ABI_VERSION = 1

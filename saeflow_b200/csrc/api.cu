@@ -254,13 +254,13 @@ struct EncodePlan {
 int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int variant, EncodePlan *pl) {
     const int64_t M = x->rows, K = x->cols, N = W->cols;
     const int wdt = W->dtype;
-    if (variant < SF_VARIANT_AUTO || variant > SF_VARIANT_SIMT)
+    if (variant < SF_VARIANT_AUTO || variant > SF_VARIANT_TCGEN05_SINGLE)
         return set_error(SF_ERR_INVALID, "unknown encode variant %d", variant);
     bool tc;
     if (wdt == SF_F32) {
         const bool tf32 = allow_tf32 || x->dtype != SF_F32;
         tc = tf32;
-        if (variant == SF_VARIANT_TCGEN05) tc = true;
+        if (variant == SF_VARIANT_TCGEN05 || variant == SF_VARIANT_TCGEN05_SINGLE) tc = true;
         if (variant == SF_VARIANT_SIMT) tc = false;
     } else {
         tc = true;
@@ -478,7 +478,7 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
         g.b = wp;
         g.b_pitch = pl.w_pitch;
     }
-    return encode_tc_dense(g, ep, s);
+    return encode_tc_dense(g, ep, variant, s);
 }
 
 int sf_row_nnz(const sf_matrix *f, int32_t *row_nnz, sf_stream stream) {

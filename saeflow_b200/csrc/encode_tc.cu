@@ -9,15 +9,23 @@
 // stored nonzeros into row_nnz (:206-208). The count is taken on the value as stored
 // (after rounding to the output dtype), so it always equals count_nonzero(out).
 //
-// Design (one persistent CTA per SM, 192 threads):
-//   warp 0      TMA producer: x tile [128 x 128 B] and W tile [256 x 128 B] per stage,
-//               SWIZZLE_128B, 4-stage mbarrier ring, no multicast.
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer, M=128 N=256, fp32
-//               accumulators double-buffered in TMEM (2 x 256 columns).
+// Two persistent, warp-specialised kernels (192 threads, one CTA per SM):
+//   warp 0      TMA producer: operand tiles of 128 B rows, SWIZZLE_128B, mbarrier ring.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer; fp32 accumulators
+//               double-buffered in TMEM (2 x 256 columns) so the epilogue of one tile
+//               overlaps the MMAs of the next.
 //   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, bias/activation in fp32,
 //               rounding, nonzero count, 16-byte streaming stores (L2 evict_first).
 //               In TOPK mode they instead keep a per-row running top-k in shared memory
 //               and write k candidates per (row, column chunk); see topk_merge_kernel.
+//
+// encode_tc2_kernel (the default for M > 128) runs on CTA pairs (cluster of 2,
+// tcgen05 cta_group::2): the pair computes a 256 x 256 tile, each CTA loading its 128 rows
+// of x and 128 columns of W_enc, so each SM pulls 64 B of operands per MMA clock instead
+// of the 96 B of the single-CTA 128 x 256 tile (encode_tc_kernel), which starves the tensor
+// cores on L2 bandwidth. Both CTAs' TMA loads complete on the leader CTA's barrier; the
+// leader's MMA thread signals each CTA's barriers with its own commit.
+//
 // The x operand is a pre-shifted copy (x - b_dec, rounded to the MMA dtype) made by
 // shift_convert_kernel: a separate HBM pass costs <1% of the GEMM, whereas shifting in
 // shared memory would compete with the tensor cores for shared-memory bandwidth.
@@ -46,6 +54,7 @@ enum Mode { kDense = 0, kTopk = 1 };
 
 struct TcParams {
     int M, N, K;
+    int bm;               // rows per tile: 128 (single CTA) or 256 (CTA pair)
     int num_m_tiles, num_n_tiles;
     int num_kb;
     int group_m;          // dense: raster group height in m-tiles
@@ -149,6 +158,82 @@ __device__ __forceinline__ void store_chunk(const TcParams &p, int row, int col0
             if (col < p.N) base[(int64_t)col * p.out_sn] = from_f32<OT>(v[j]);
         }
     }
+}
+
+// Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
+__device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int mode, int et, int n_blk, int buf) {
+    for (int j = et; j < kBN; j += 128) {
+        const int col = n_blk * kBN + j;
+        float b = 0.f, t = 0.f;
+        if (col < p.N) {
+            b = load_as_f32(p.b_enc, p.b_enc_dtype, (int64_t)col * p.b_enc_stride);
+            if (mode == kDense && p.activation == SF_ACT_JUMPRELU)
+                t = load_as_f32(p.thr, p.thr_dtype, (int64_t)col * p.thr_stride);
+        }
+        sh->bias[buf][j] = b;
+        sh->thr[buf][j] = t;
+    }
+}
+
+// One tile of epilogue for this thread's row: reads the 256 fp32 accumulators of TMEM lane
+// (taddr's lane) 32 columns at a time; `release` runs once all TMEM reads of the tile are
+// complete, so the MMA warp may overwrite the accumulator buffer.
+template <int MODE, typename Release>
+__device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
+                                              int et, int row, int n_blk, int buf, uint32_t taddr, uint64_t pol_out,
+                                              unsigned long long &min_key, int &min_slot, Release release) {
+    int cnt = 0;
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, r);
+        tmem_ld_wait();
+        if (c == kBN / 32 - 1) release();
+        const int col0 = n_blk * kBN + c * 32;
+        if (MODE == kDense) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
+                float o = fmaxf(pre, 0.f);
+                if (p.activation == SF_ACT_JUMPRELU) o = (pre > sh->thr[buf][c * 32 + j]) ? o : 0.f;
+                o = round_to(o, p.out_dtype);
+                v[j] = o;
+                cnt += (o != 0.f && col0 + j < p.N) ? 1 : 0;
+            }
+            if (row < p.M) {
+                if (p.out_dtype == SF_BF16)
+                    store_chunk<__nv_bfloat16>(p, row, col0, v, pol_out);
+                else if (p.out_dtype == SF_F16)
+                    store_chunk<__half>(p, row, col0, v, pol_out);
+                else
+                    store_chunk<float>(p, row, col0, v, pol_out);
+            }
+        } else {
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) {
+                const int col = col0 + j;
+                if (col >= p.N) break;
+                const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
+                const float o = round_to(fmaxf(pre, 0.f), p.values_dtype);
+                const unsigned long long key =
+                    (static_cast<unsigned long long>(__float_as_uint(o) & 0x7FFFFFFFu) << 32) |
+                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
+                if (key > min_key) {
+                    topk_lists[min_slot * 128 + et] = key;
+                    min_key = ~0ull;
+                    for (int s = 0; s < p.k; ++s) {
+                        const unsigned long long q = topk_lists[s * 128 + et];
+                        if (q < min_key) {
+                            min_key = q;
+                            min_slot = s;
+                        }
+                    }
+                }
+            }
+        }
+    }
+    if (MODE == kDense && p.row_nnz != nullptr && row < p.M && cnt != 0) atomicAdd(p.row_nnz + row, cnt);
 }
 
 template <int AB_FMT, bool B_MN, int MODE, int STAGES>
@@ -319,81 +404,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int nt = 0; nt < un.n_count; ++nt, ++tile_iter) {
                 const int n_blk = un.n_first + nt;
                 const int buf = tile_iter & 1;
-                // Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
-                for (int j = et; j < kBN; j += 128) {
-                    const int col = n_blk * kBN + j;
-                    float b = 0.f, t = 0.f;
-                    if (col < p.N) {
-                        b = load_as_f32(p.b_enc, p.b_enc_dtype, (int64_t)col * p.b_enc_stride);
-                        if (MODE == kDense && p.activation == SF_ACT_JUMPRELU)
-                            t = load_as_f32(p.thr, p.thr_dtype, (int64_t)col * p.thr_stride);
-                    }
-                    sh->bias[buf][j] = b;
-                    sh->thr[buf][j] = t;
-                }
+                stage_bias(p, sh, MODE, et, n_blk, buf);
                 named_bar_sync(1, 128);
-
                 if (!mbar_wait(&sh->tmem_full[acc], acc_phase, abort_flag, p.err)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
-                int cnt = 0;
-#pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + c * 32, r);
-                    tmem_ld_wait();
-                    if (c == kBN / 32 - 1) {
-                        tc_fence_before();
-                        mbar_arrive(&sh->tmem_empty[acc]);
-                    }
-                    const int col0 = n_blk * kBN + c * 32;
-                    if (MODE == kDense) {
-                        float v[32];
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
-                            float o = fmaxf(pre, 0.f);
-                            if (p.activation == SF_ACT_JUMPRELU) o = (pre > sh->thr[buf][c * 32 + j]) ? o : 0.f;
-                            o = round_to(o, p.out_dtype);
-                            v[j] = o;
-                            cnt += (o != 0.f && col0 + j < p.N) ? 1 : 0;
-                        }
-                        if (row < p.M) {
-                            if (p.out_dtype == SF_BF16)
-                                store_chunk<__nv_bfloat16>(p, row, col0, v, pol_out);
-                            else if (p.out_dtype == SF_F16)
-                                store_chunk<__half>(p, row, col0, v, pol_out);
-                            else
-                                store_chunk<float>(p, row, col0, v, pol_out);
-                        }
-                    } else {
-#pragma unroll 4
-                        for (int j = 0; j < 32; ++j) {
-                            const int col = col0 + j;
-                            if (col >= p.N) break;
-                            const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
-                            const float o = round_to(fmaxf(pre, 0.f), p.values_dtype);
-                            const unsigned long long key =
-                                (static_cast<unsigned long long>(__float_as_uint(o) & 0x7FFFFFFFu) << 32) |
-                                static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
-                            if (key > min_key) {
-                                topk_lists[min_slot * 128 + et] = key;
-                                min_key = ~0ull;
-                                for (int s = 0; s < p.k; ++s) {
-                                    const unsigned long long q = topk_lists[s * 128 + et];
-                                    if (q < min_key) {
-                                        min_key = q;
-                                        min_slot = s;
-                                    }
-                                }
-                            }
-                        }
-                    }
-                }
-                if (MODE == kDense && p.row_nnz != nullptr && row < p.M && cnt != 0) atomicAdd(p.row_nnz + row, cnt);
+                const int acc_now = acc;
+                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key, min_slot, [&] {
+                    tc_fence_before();
+                    mbar_arrive(&sh->tmem_empty[acc_now]);
+                });
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
@@ -412,6 +435,239 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// -------------------------------------------------------------------------------------
+// CTA-pair kernel (cluster of 2, tcgen05 cta_group::2): 256 x 256 tile per pair.
+template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    encode_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const TcParams p) {
+    constexpr int ES = (AB_FMT == 2) ? 4 : 2;
+    constexpr int BK = 128 / ES;
+    constexpr int UMMA_K = 32 / ES;
+    constexpr int KSTEPS = BK / UMMA_K;
+    constexpr int MN_BOX = 128 / ES;
+    constexpr int MN_BOX_BYTES = BK * 128;
+    constexpr int HALF_N = kBN / 2;            // columns of W_enc this CTA holds per stage
+    constexpr int A_BYTES = 128 * 128;         // 128 rows x 128 B
+    constexpr int B_BYTES = HALF_N * 128;      // 128 columns x 128 B
+    constexpr uint32_t PAIR_TX = 2u * (A_BYTES + B_BYTES);
+    constexpr uint32_t IDESC = make_idesc(AB_FMT, B_MN, 256, kBN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + STAGES * A_BYTES;
+    TcShared *sh = reinterpret_cast<TcShared *>(smem + STAGES * (A_BYTES + B_BYTES));
+    unsigned long long *topk_lists = reinterpret_cast<unsigned long long *>(sh + 1);  // [k][128]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = (int)cluster_id_x();
+    const int npairs = (int)num_clusters_x();
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&sh->full[s], 1);   // leader's: its expect_tx arrive + both CTAs' bytes
+            mbar_init(&sh->empty[s], 1);  // one commit from the leader's MMA thread
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sh->tmem_full[b], 1);
+            mbar_init(&sh->tmem_empty[b], 8);  // leader's: one arrive per epilogue warp of both CTAs
+        }
+        mbar_init(&sh->drain, 1);
+        sh->abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&sh->tmem_base, kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = sh->tmem_base;
+    volatile int *abort_flag = &sh->abort_flag;
+    const uint32_t peer_abort = map_to_rank(smem_u32(&sh->abort_flag), rank ^ 1u);
+    // A wait that runs out (or sees the abort flag) also raises the other CTA's flag.
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (mbar_wait(bar, parity, abort_flag, p.err)) return true;
+        st_remote_u32(peer_abort, 1u);
+        return false;
+    };
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer (both CTAs)
+        if (lane == 0) {
+            const uint64_t pol_x = l2_policy_evict_last();
+            const uint64_t pol_w = l2_policy_evict_normal();
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, armed_parity = 0;
+            bool ok = true;
+            for (int u = pair; ok && u < p.num_units; u += npairs) {
+                const Unit un = unit_coords(p, u, MODE);
+                for (int nt = 0; ok && nt < un.n_count; ++nt) {
+                    const int n_blk = un.n_first + nt;
+                    for (int kb = 0; kb < p.num_kb; ++kb) {
+                        if (!wait(&sh->empty[stage], phase ^ 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t full_leader = map_to_rank(smem_u32(&sh->full[stage]), 0);
+                        if (leader) {
+                            mbar_arrive_expect_tx(&sh->full[stage], PAIR_TX);
+                            armed |= 1u << stage;
+                            armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
+                        }
+                        tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_leader, kb * BK,
+                                         un.m_blk * 256 + (int)rank * 128, pol_x);
+                        uint8_t *b_dst = sB + stage * B_BYTES;
+                        const int n0 = n_blk * kBN + (int)rank * HALF_N;
+                        if (B_MN) {
+#pragma unroll
+                            for (int j = 0; j < HALF_N / MN_BOX; ++j)
+                                tma_load_2d_pair(b_dst + j * MN_BOX_BYTES, &tmB, full_leader, n0 + j * MN_BOX,
+                                                 kb * BK, pol_w);
+                        } else {
+                            tma_load_2d_pair(b_dst, &tmB, full_leader, kb * BK, n0, pol_w);
+                        }
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                }
+            }
+            if (*abort_flag) {
+                if (leader) {
+                    // Both CTAs' copies of every armed stage complete on these barriers.
+                    for (int s = 0; s < STAGES; ++s)
+                        if (armed & (1u << s)) mbar_drain(&sh->full[s], (armed_parity >> s) & 1u, p.err);
+                } else {
+                    // This CTA's copies complete on the leader's barriers: give them time to land.
+                    const unsigned long long t0 = global_timer_ns();
+                    while (global_timer_ns() - t0 < 2000000ull) __nanosleep(1000);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer (leader only)
+        if (leader && lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            bool ok = true;
+            for (int u = pair; ok && u < p.num_units; u += npairs) {
+                const Unit un = unit_coords(p, u, MODE);
+                for (int nt = 0; ok && nt < un.n_count; ++nt) {
+                    if (!wait(&sh->tmem_empty[acc], acc_phase ^ 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + acc * kAccCols;
+                    for (int kb = 0; kb < p.num_kb; ++kb) {
+                        if (!wait(&sh->full[stage], phase)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+                        const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+                        for (int ks = 0; ks < KSTEPS; ++ks) {
+                            const uint64_t ad = smem_desc_sw128(a_addr + ks * 32, 16, 1024);
+                            const uint64_t bd = B_MN ? smem_desc_sw128(b_addr + ks * UMMA_K * 128, MN_BOX_BYTES, 1024)
+                                                     : smem_desc_sw128(b_addr + ks * 32, 16, 1024);
+                            const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
+                            if (AB_FMT == 2)
+                                umma_tf32_pair(d_tmem, ad, bd, IDESC, accum);
+                            else
+                                umma_f16_pair(d_tmem, ad, bd, IDESC, accum);
+                        }
+                        const uint32_t e_off = smem_u32(&sh->empty[stage]);
+                        umma_commit_pair(map_to_rank(e_off, 0));
+                        umma_commit_pair(map_to_rank(e_off, 1));
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    const uint32_t f_off = smem_u32(&sh->tmem_full[acc]);
+                    umma_commit_pair(map_to_rank(f_off, 0));
+                    umma_commit_pair(map_to_rank(f_off, 1));
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_phase ^= 1u;
+                    }
+                }
+            }
+            umma_commit_pair(map_to_rank(smem_u32(&sh->drain), 0));
+            mbar_drain(&sh->drain, 0, p.err);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue (both CTAs)
+        const int et = threadIdx.x - 64;
+        const int quad = warp & 3;
+        const int row_in_tile = (int)rank * 128 + quad * 32 + lane;
+        const uint64_t pol_out = l2_policy_evict_first();
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        int tile_iter = 0;
+        bool ok = true;
+        for (int u = pair; ok && u < p.num_units; u += npairs) {
+            const Unit un = unit_coords(p, u, MODE);
+            const int row = un.m_blk * 256 + row_in_tile;
+            unsigned long long min_key = 0;
+            int min_slot = 0;
+            if (MODE == kTopk) {
+                for (int s = 0; s < p.k; ++s) topk_lists[s * 128 + et] = 0ull;
+            }
+            for (int nt = 0; nt < un.n_count; ++nt, ++tile_iter) {
+                const int n_blk = un.n_first + nt;
+                const int buf = tile_iter & 1;
+                stage_bias(p, sh, MODE, et, n_blk, buf);
+                named_bar_sync(1, 128);
+                if (!wait(&sh->tmem_full[acc], acc_phase)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
+                const uint32_t empty_leader = map_to_rank(smem_u32(&sh->tmem_empty[acc]), 0);
+                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key, min_slot, [&] {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(empty_leader);
+                });
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+            if (MODE == kTopk && ok && row < p.M) {
+                unsigned long long *dst = p.cand + ((int64_t)row * p.n_chunks + un.chunk) * p.k;
+                for (int s = 0; s < p.k; ++s) dst[s] = topk_lists[s * 128 + et];
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the leader's MMAs no longer read this CTA's shared memory
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -451,8 +707,8 @@ int make_map_2d(CUtensorMap *map, const void *base, int ab_fmt, uint64_t inner, 
 }
 
 template <int AB_FMT, bool B_MN, int MODE, int STAGES>
-int launch_typed(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
-                 cudaStream_t stream) {
+int launch_single(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
+                  cudaStream_t stream) {
     auto kern = encode_tc_kernel<AB_FMT, B_MN, MODE, STAGES>;
     const size_t smem = 1024 + (size_t)STAGES * kStageBytes + sizeof(TcShared) + extra_smem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -462,18 +718,47 @@ int launch_typed(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams 
     return check_cuda(cudaGetLastError(), "encode_tc launch");
 }
 
-template <int MODE, int STAGES>
-int dispatch(int ab_fmt, bool b_mn, const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
-             size_t extra_smem, cudaStream_t s) {
-    if (ab_fmt == 1) return b_mn ? launch_typed<1, true, MODE, STAGES>(tmA, tmB, p, extra_smem, s)
-                                 : launch_typed<1, false, MODE, STAGES>(tmA, tmB, p, extra_smem, s);
-    if (ab_fmt == 0) return b_mn ? launch_typed<0, true, MODE, STAGES>(tmA, tmB, p, extra_smem, s)
-                                 : launch_typed<0, false, MODE, STAGES>(tmA, tmB, p, extra_smem, s);
-    return b_mn ? launch_typed<2, true, MODE, STAGES>(tmA, tmB, p, extra_smem, s)
-                : launch_typed<2, false, MODE, STAGES>(tmA, tmB, p, extra_smem, s);
+template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+int launch_pair(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
+                cudaStream_t stream) {
+    auto kern = encode_tc2_kernel<AB_FMT, B_MN, MODE, STAGES>;
+    const size_t smem = 1024 + (size_t)STAGES * (kBM * 128 + (kBN / 2) * 128) + sizeof(TcShared) + extra_smem;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(encode_tc2)");
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(2 * std::max(1, num_sms() / 2));
+    const int pairs = pair_slots(reinterpret_cast<const void *>(kern), cfg);
+    cfg.gridDim = dim3(2 * std::max(1, std::min(p.num_units, pairs)));
+    e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, p);
+    if (e != cudaSuccess) return check_cuda(e, "encode_tc2 launch");
+    return check_cuda(cudaGetLastError(), "encode_tc2 launch");
 }
 
-int build_maps(const GemmOperands &g, CUtensorMap *tmA, CUtensorMap *tmB) {
+template <int MODE, int STAGES, bool PAIR>
+int dispatch(int ab_fmt, bool b_mn, const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
+             size_t extra_smem, cudaStream_t s) {
+#define SF_LAUNCH(F, MN) \
+    (PAIR ? launch_pair<F, MN, MODE, STAGES>(tmA, tmB, p, extra_smem, s) \
+          : launch_single<F, MN, MODE, STAGES>(tmA, tmB, p, extra_smem, s))
+    if (ab_fmt == 1) return b_mn ? SF_LAUNCH(1, true) : SF_LAUNCH(1, false);
+    if (ab_fmt == 0) return b_mn ? SF_LAUNCH(0, true) : SF_LAUNCH(0, false);
+    return b_mn ? SF_LAUNCH(2, true) : SF_LAUNCH(2, false);
+#undef SF_LAUNCH
+}
+
+// Tensor maps: A boxes of 128 rows; B boxes of 256 (single CTA) or 128 (per CTA of a pair)
+// columns when K-major, 128 B x BK rows when MN-major.
+int build_maps(const GemmOperands &g, bool pair, CUtensorMap *tmA, CUtensorMap *tmB) {
     const int es = g.ab_fmt == 2 ? 4 : 2;
     const uint32_t bk = 128 / es;
     int st = make_map_2d(tmA, g.a, g.ab_fmt, (uint64_t)g.K, (uint64_t)g.M, (uint64_t)g.a_pitch * es, bk, kBM);
@@ -481,15 +766,17 @@ int build_maps(const GemmOperands &g, CUtensorMap *tmA, CUtensorMap *tmB) {
     if (g.b_mn_major)  // W[k, n] at b + k*b_pitch + n
         return make_map_2d(tmB, g.b, g.ab_fmt, (uint64_t)g.N, (uint64_t)g.K, (uint64_t)g.b_pitch * es, 128 / es, bk);
     // W[k, n] at b + n*b_pitch + k
-    return make_map_2d(tmB, g.b, g.ab_fmt, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.b_pitch * es, bk, kBN);
+    return make_map_2d(tmB, g.b, g.ab_fmt, (uint64_t)g.K, (uint64_t)g.N, (uint64_t)g.b_pitch * es, bk,
+                       pair ? kBN / 2 : kBN);
 }
 
-void fill_common(TcParams &p, const GemmOperands &g, unsigned *err) {
+void fill_common(TcParams &p, const GemmOperands &g, bool pair, unsigned *err) {
     const int es = g.ab_fmt == 2 ? 4 : 2;
     p.M = (int)g.M;
     p.N = (int)g.N;
     p.K = (int)g.K;
-    p.num_m_tiles = (int)((g.M + kBM - 1) / kBM);
+    p.bm = pair ? 256 : kBM;
+    p.num_m_tiles = (int)((g.M + p.bm - 1) / p.bm);
     p.num_n_tiles = (int)((g.N + kBN - 1) / kBN);
     p.num_kb = (int)((g.K + (128 / es) - 1) / (128 / es));
     p.err = err;
@@ -497,15 +784,44 @@ void fill_common(TcParams &p, const GemmOperands &g, unsigned *err) {
 
 }  // namespace
 
-int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, cudaStream_t stream) {
+// Pairs of SMs that can hold one pair-kernel cluster each (cached per kernel).
+int pair_slots(const void *kern, const cudaLaunchConfig_t &cfg) {
+    static std::mutex mu;
+    static const void *keys[64];
+    static int vals[64];
+    static int n = 0;
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < n; ++i)
+        if (keys[i] == kern) return vals[i];
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = std::max(1, num_sms() / 2);
+    }
+    if (n < 64) {
+        keys[n] = kern;
+        vals[n] = clusters;
+        ++n;
+    }
+    return clusters;
+}
+
+// The CTA-pair kernel needs more than one 128-row tile to pay off.
+static bool use_pair(const GemmOperands &g, int variant) {
+    if (variant == SF_VARIANT_TCGEN05_SINGLE) return false;
+    return g.M > kBM;
+}
+
+int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, cudaStream_t stream) {
+    const bool pair = use_pair(g, variant);
     CUtensorMap tmA, tmB;
-    int st = build_maps(g, &tmA, &tmB);
+    int st = build_maps(g, pair, &tmA, &tmB);
     if (st) return st;
     TcParams p{};
-    fill_common(p, g, device_error_word());
+    fill_common(p, g, pair, device_error_word());
     // x (A) stays L2-resident when a group of m-tiles fits in ~64 MB.
     const int es = g.ab_fmt == 2 ? 4 : 2;
-    const int64_t a_tile_bytes = (int64_t)kBM * g.K * es;
+    const int64_t a_tile_bytes = (int64_t)p.bm * g.K * es;
     p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, (64ll << 20) / std::max<int64_t>(1, a_tile_bytes)));
     p.num_units = p.num_m_tiles * p.num_n_tiles;
     p.n_chunks = 1;
@@ -523,23 +839,26 @@ int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, cudaStream_t 
     p.out_sn = ep.out_sn;
     p.out_vec = ep.out_vec;
     p.row_nnz = ep.row_nnz;
-    return dispatch<kDense, 4>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
+    if (pair) return dispatch<kDense, 6, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
+    return dispatch<kDense, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
 }
 
 // Column chunks per row for the top-k schedule: enough (m-tile, chunk) units to fill the
-// SMs in whole waves.
+// available CTAs (or CTA pairs) in whole waves.
 int topk_chunks(int64_t M, int64_t N) {
-    const int m_tiles = (int)((M + kBM - 1) / kBM);
+    const bool pair = M > kBM;
+    const int bm = pair ? 256 : kBM;
+    const int m_tiles = (int)((M + bm - 1) / bm);
     const int n_tiles = (int)((N + kBN - 1) / kBN);
-    const int sms = num_sms();
+    const int slots = pair ? std::max(1, num_sms() / 2) : num_sms();
     int best = 1;
     double best_eff = -1.0;
     for (int c = 1; c <= std::min(n_tiles, 32); ++c) {
         const int tpc = (n_tiles + c - 1) / c;
         const int chunks = (n_tiles + tpc - 1) / tpc;
         const long units = (long)m_tiles * chunks;
-        const long waves = (units + sms - 1) / sms;
-        double eff = (double)units / (double)(waves * sms);
+        const long waves = (units + slots - 1) / slots;
+        double eff = (double)units / (double)(waves * slots);
         eff -= 0.002 * c;  // prefer fewer candidates at equal balance
         if (eff > best_eff + 1e-9) {
             best_eff = eff;
@@ -550,11 +869,12 @@ int topk_chunks(int64_t M, int64_t N) {
 }
 
 int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t stream) {
+    const bool pair = g.M > kBM;  // must match topk_chunks
     CUtensorMap tmA, tmB;
-    int st = build_maps(g, &tmA, &tmB);
+    int st = build_maps(g, pair, &tmA, &tmB);
     if (st) return st;
     TcParams p{};
-    fill_common(p, g, device_error_word());
+    fill_common(p, g, pair, device_error_word());
     p.group_m = 1;
     const int chunks = tk.n_chunks;
     p.tiles_per_chunk = (p.num_n_tiles + chunks - 1) / chunks;
@@ -570,8 +890,13 @@ int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t strea
     p.cand = tk.cand;
     if (tk.k < 1 || tk.k > kTopkMaxK) return set_error(SF_ERR_UNSUPPORTED, "fused top-k supports 1 <= k <= %d", kTopkMaxK);
     const size_t lists = (size_t)tk.k * 128 * sizeof(unsigned long long);
-    if (tk.k <= 64) return dispatch<kTopk, 3>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
-    return dispatch<kTopk, 2>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+    if (pair) {
+        if (tk.k <= 32) return dispatch<kTopk, 4, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+        if (tk.k <= 64) return dispatch<kTopk, 4, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+        return dispatch<kTopk, 3, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+    }
+    if (tk.k <= 64) return dispatch<kTopk, 3, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+    return dispatch<kTopk, 2, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
 }
 
 }  // namespace sf

@@ -46,7 +46,8 @@ struct TopkArgs {
     unsigned long long *cand;  // [M, n_chunks, k]
 };
 
-int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, cudaStream_t stream);
+int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, cudaStream_t stream);
+int pair_slots(const void *kern, const cudaLaunchConfig_t &cfg);
 int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t stream);
 int topk_chunks(int64_t M, int64_t N);
 constexpr int kTopkMaxK = 120;  // shared-memory bound of the fused top-k lists

@@ -23,10 +23,13 @@ from .. import _abi
 ACTIVATIONS = {"relu": _abi.SF_ACT_RELU, "jumprelu": _abi.SF_ACT_JUMPRELU}
 
 # Tile shapes of the two kernels, reported by best_config().
-TCGEN05_CONFIG = {"variant": "tcgen05", "BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K_BYTES": 128, "stages": 4,
-                  "tmem_accumulators": 2}
+TCGEN05_PAIR_CONFIG = {"variant": "tcgen05", "BLOCK_M": 256, "BLOCK_N": 256, "BLOCK_K_BYTES": 128, "stages": 6,
+                       "cta_pair": True, "tmem_accumulators": 2}
+TCGEN05_CONFIG = {"variant": "tcgen05_1cta", "BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K_BYTES": 128, "stages": 4,
+                  "cta_pair": False, "tmem_accumulators": 2}
 SIMT_CONFIG = {"variant": "simt", "BLOCK_M": 128, "BLOCK_N": 128, "BLOCK_K": 8}
-_VARIANTS = {"auto": _abi.SF_VARIANT_AUTO, "tcgen05": _abi.SF_VARIANT_TCGEN05, "simt": _abi.SF_VARIANT_SIMT}
+_VARIANTS = {"auto": _abi.SF_VARIANT_AUTO, "tcgen05": _abi.SF_VARIANT_TCGEN05, "simt": _abi.SF_VARIANT_SIMT,
+             "tcgen05_1cta": _abi.SF_VARIANT_TCGEN05_SINGLE}
 
 _last_config = None
 
@@ -46,7 +49,7 @@ def _variant(config) -> int:
 
 
 def _uses_tensor_cores(x, W_enc, allow_tf32, variant) -> bool:
-    if variant == _abi.SF_VARIANT_TCGEN05:
+    if variant in (_abi.SF_VARIANT_TCGEN05, _abi.SF_VARIANT_TCGEN05_SINGLE):
         return True
     if variant == _abi.SF_VARIANT_SIMT:
         return False
@@ -60,7 +63,7 @@ def fused_encode(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *,
     x: [M, d_in] fp32 / bf16 / fp16. W_enc: [d_in, d_sae], any strides.
     activation: "relu" or "jumprelu" (needs `threshold` [d_sae]).
     row_nnz: optional zeroed int32 [M] buffer; receives each row's nonzero count.
-    config: {"variant": "auto" | "tcgen05" | "simt"} to pin the kernel.
+    config: {"variant": "auto" | "tcgen05" | "tcgen05_1cta" | "simt"} to pin the kernel.
     allow_tf32: fp32 inputs only; defaults to torch.backends.cuda.matmul.allow_tf32.
     """
     global _last_config
@@ -96,7 +99,12 @@ def fused_encode(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *,
             ctypes.byref(xm), ctypes.byref(wm), _abi.ref(be), _abi.ref(bd), _abi.ref(th), ACTIVATIONS[activation],
             ctypes.byref(om), row_nnz.data_ptr() if row_nnz is not None else None, int(bool(allow_tf32)), variant,
             ws.data_ptr(), ws.numel(), _abi.stream_of(dev)))
-    _last_config = dict(TCGEN05_CONFIG if _uses_tensor_cores(x, W_enc, allow_tf32, variant) else SIMT_CONFIG)
+    if not _uses_tensor_cores(x, W_enc, allow_tf32, variant):
+        _last_config = dict(SIMT_CONFIG)
+    elif M > 128 and variant != _abi.SF_VARIANT_TCGEN05_SINGLE:
+        _last_config = dict(TCGEN05_PAIR_CONFIG)
+    else:
+        _last_config = dict(TCGEN05_CONFIG)
     return out
 
 

@@ -95,6 +95,26 @@ def test_fused_encode_weight_layouts_tcgen05(dtype, layout):
     check_encode(got, x, W, sae.b_enc, sae.b_dec, sae.threshold, "jumprelu", row_nnz)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(129, 64, 256), (300, 200, 700), (1000, 512, 3000), (513, 2304, 1024)])
+@pytest.mark.parametrize("colmajor", [False, True])
+def test_cta_pair_kernel_matches_single_cta_kernel(dtype, shape, colmajor):
+    """The CTA-pair tcgen05 kernel (256 x 256 tiles) and the single-CTA one agree, and both
+    match the oracle; shapes leave partial pair tiles in M and N."""
+    M, d_in, d_sae = shape
+    sae = make_sae(d_in, d_sae, "jumprelu", dtype).to("cuda")
+    W = sae.W_enc.T.contiguous().T if colmajor else sae.W_enc
+    x = torch.randn(M, d_in, device="cuda").to(dtype)
+    outs = []
+    for variant in ("tcgen05", "tcgen05_1cta"):
+        row_nnz = torch.zeros(M, device="cuda", dtype=torch.int32)
+        got = fused_encode(x, W, sae.b_enc, sae.b_dec, sae.threshold, "jumprelu", row_nnz=row_nnz,
+                           config={"variant": variant})
+        check_encode(got, x, W, sae.b_enc, sae.b_dec, sae.threshold, "jumprelu", row_nnz)
+        outs.append(got.float())
+    torch.testing.assert_close(outs[0], outs[1], atol=TOL[dtype], rtol=TOL[dtype])
+
+
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_fused_encode_out_dtype(out_dtype):
     sae = make_sae(96, 300, "relu", torch.bfloat16).to("cuda")
