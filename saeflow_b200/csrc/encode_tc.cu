@@ -136,30 +136,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity, unsig
     }
 }
 
-template <typename OT>
-__device__ __forceinline__ void store_chunk(const TcParams &p, int row, int col0, const float (&v)[32],
-                                            uint64_t policy) {
-    OT *base = reinterpret_cast<OT *>(p.out) + (int64_t)row * p.out_sm;
-    if (p.out_vec && col0 + 32 <= p.N) {
-        constexpr int EPV = 16 / sizeof(OT);
-        OT *dst = base + col0;
-#pragma unroll
-        for (int j = 0; j < 32; j += EPV) {
-            uint4 pk;
-            OT *e = reinterpret_cast<OT *>(&pk);
-#pragma unroll
-            for (int t = 0; t < EPV; ++t) e[t] = from_f32<OT>(v[j + t]);
-            st_global_v4_hint(dst + j, pk, policy);
-        }
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int col = col0 + j;
-            if (col < p.N) base[(int64_t)col * p.out_sn] = from_f32<OT>(v[j]);
-        }
-    }
-}
-
 // Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
 __device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int mode, int et, int n_blk, int buf) {
     for (int j = et; j < kBN; j += 128) {
@@ -175,65 +151,214 @@ __device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int 
     }
 }
 
-// One tile of epilogue for this thread's row: reads the 256 fp32 accumulators of TMEM lane
-// (taddr's lane) 32 columns at a time; `release` runs once all TMEM reads of the tile are
-// complete, so the MMA warp may overwrite the accumulator buffer.
-template <int MODE, typename Release>
-__device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
-                                              int et, int row, int n_blk, int buf, uint32_t taddr, uint64_t pol_out,
-                                              unsigned long long &min_key, int &min_slot, Release release) {
-    int cnt = 0;
-#pragma unroll 1
-    for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_ld_wait();
-        if (c == kBN / 32 - 1) release();
-        const int col0 = n_blk * kBN + c * 32;
-        if (MODE == kDense) {
-            float v[32];
+// Packs two fp32 values to the 16-bit output type (round to nearest even); returns the bits.
+template <typename OT>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Dense epilogue of one 32-column chunk: bias, activation, rounding to OT, nonzero count on
+// the stored bits, 16-byte stores. FULL: all 32 columns are inside d_sae.
+template <typename OT, bool JUMP, bool FULL>
+__device__ __forceinline__ void dense_chunk(const TcParams &p, const float *bias, const float *thr,
+                                            const uint32_t (&r)[32], int row, int col0, uint64_t pol_out,
+                                            int &cnt) {
+    float o[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
-                float o = fmaxf(pre, 0.f);
-                if (p.activation == SF_ACT_JUMPRELU) o = (pre > sh->thr[buf][c * 32 + j]) ? o : 0.f;
-                o = round_to(o, p.out_dtype);
-                v[j] = o;
-                cnt += (o != 0.f && col0 + j < p.N) ? 1 : 0;
+    for (int j = 0; j < 32; j += 4) {
+        const float4 b4 = *reinterpret_cast<const float4 *>(bias + j);
+        float4 t4;
+        if (JUMP) t4 = *reinterpret_cast<const float4 *>(thr + j);
+        const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+        const float tt[4] = {JUMP ? t4.x : 0.f, JUMP ? t4.y : 0.f, JUMP ? t4.z : 0.f, JUMP ? t4.w : 0.f};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float pre = __uint_as_float(r[j + e]) + bb[e];
+            float v = fmaxf(pre, 0.f);
+            if (JUMP) v = (pre > tt[e]) ? v : 0.f;
+            o[j + e] = (FULL || col0 + j + e < p.N) ? v : 0.f;
+        }
+    }
+    OT *base = reinterpret_cast<OT *>(p.out) + (int64_t)row * p.out_sm;
+    if constexpr (sizeof(OT) == 2) {
+        uint32_t pk[16];
+        uint32_t nz2 = 0;  // per-halfword nonzero counts
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            pk[j] = pack2<OT>(o[2 * j], o[2 * j + 1]);
+            nz2 += __vsetne2(pk[j] & 0x7FFF7FFFu, 0u);
+        }
+        cnt += (int)(nz2 & 0xFFFFu) + (int)(nz2 >> 16);
+        if (row < p.M) {
+            if (FULL && p.out_vec) {
+#pragma unroll
+                for (int j = 0; j < 16; j += 4)
+                    st_global_v4_hint(base + col0 + 2 * j, make_uint4(pk[j], pk[j + 1], pk[j + 2], pk[j + 3]),
+                                      pol_out);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (!FULL && col0 + j >= p.N) break;
+                    const uint16_t bits = (j & 1) ? (uint16_t)(pk[j >> 1] >> 16) : (uint16_t)(pk[j >> 1] & 0xFFFFu);
+                    reinterpret_cast<uint16_t *>(base)[(int64_t)(col0 + j) * p.out_sn] = bits;
+                }
             }
-            if (row < p.M) {
-                if (p.out_dtype == SF_BF16)
-                    store_chunk<__nv_bfloat16>(p, row, col0, v, pol_out);
-                else if (p.out_dtype == SF_F16)
-                    store_chunk<__half>(p, row, col0, v, pol_out);
-                else
-                    store_chunk<float>(p, row, col0, v, pol_out);
-            }
-        } else {
-#pragma unroll 4
-            for (int j = 0; j < 32; ++j) {
-                const int col = col0 + j;
-                if (col >= p.N) break;
-                const float pre = __uint_as_float(r[j]) + sh->bias[buf][c * 32 + j];
-                const float o = round_to(fmaxf(pre, 0.f), p.values_dtype);
-                const unsigned long long key =
-                    (static_cast<unsigned long long>(__float_as_uint(o) & 0x7FFFFFFFu) << 32) |
-                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
-                if (key > min_key) {
-                    topk_lists[min_slot * 128 + et] = key;
-                    min_key = ~0ull;
-                    for (int s = 0; s < p.k; ++s) {
-                        const unsigned long long q = topk_lists[s * 128 + et];
-                        if (q < min_key) {
-                            min_key = q;
-                            min_slot = s;
-                        }
-                    }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) cnt += (o[j] != 0.f) ? 1 : 0;
+        if (row < p.M) {
+            if (FULL && p.out_vec) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    st_global_v4_hint(base + col0 + j,
+                                      make_uint4(__float_as_uint(o[j]), __float_as_uint(o[j + 1]),
+                                                 __float_as_uint(o[j + 2]), __float_as_uint(o[j + 3])),
+                                      pol_out);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (!FULL && col0 + j >= p.N) break;
+                    reinterpret_cast<float *>(base)[(int64_t)(col0 + j) * p.out_sn] = o[j];
                 }
             }
         }
     }
+}
+
+// Replaces this thread's smallest list entry (slot `slot`) by `key` and returns the new
+// smallest entry. Rare after the first tiles of a unit, so kept out of line.
+struct MinEntry {
+    unsigned long long key;
+    int slot;
+};
+__device__ __noinline__ MinEntry topk_insert(unsigned long long *topk_lists, int et, int k, int slot,
+                                             unsigned long long key) {
+    topk_lists[slot * 128 + et] = key;
+    MinEntry m{~0ull, 0};
+    for (int s = 0; s < k; ++s) {
+        const unsigned long long q = topk_lists[s * 128 + et];
+        if (q < m.key) {
+            m.key = q;
+            m.slot = s;
+        }
+    }
+    return m;
+}
+
+__device__ __forceinline__ float min_value_of(unsigned long long min_key) {
+    // An empty slot (key 0) lets every value in.
+    return min_key == 0ull ? -1.f : __uint_as_float(static_cast<uint32_t>(min_key >> 32));
+}
+
+// Top-k epilogue of one 32-column chunk: values are compared against the current k-th
+// largest in fp32 first (rounding is monotonic, so a value not above it cannot enter), and
+// only survivors build the packed (value, ~column) key.
+__device__ __forceinline__ void topk_chunk(const TcParams &p, const float *bias, const uint32_t (&r)[32], int col0,
+                                           unsigned long long *topk_lists, int et, unsigned long long &min_key,
+                                           int &min_slot) {
+    float min_val = min_value_of(min_key);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int col = col0 + j;
+        const float o = fmaxf(__uint_as_float(r[j]) + bias[j], 0.f);
+        if (o > min_val && col < p.N) {
+            const float v = round_to(o, p.values_dtype);
+            const unsigned long long key =
+                (static_cast<unsigned long long>(__float_as_uint(v) & 0x7FFFFFFFu) << 32) |
+                static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
+            if (key > min_key) {
+                const MinEntry m = topk_insert(topk_lists, et, p.k, min_slot, key);
+                min_key = m.key;
+                min_slot = m.slot;
+                min_val = min_value_of(min_key);
+            }
+        }
+    }
+}
+
+// One tile of epilogue for this thread's row: reads the 256 fp32 accumulators of its TMEM
+// lane 32 columns at a time, loading chunk c+1 while chunk c is processed; `release` runs
+// once all TMEM reads of the tile are complete, so the MMA warp may reuse the buffer.
+template <int MODE, typename OT, bool JUMP, typename Release>
+__device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
+                                                int et, int row, int n_blk, int buf, uint32_t taddr,
+                                                uint64_t pol_out, unsigned long long &min_key, int &min_slot,
+                                                Release release) {
+    constexpr int NC = kBN / 32;
+    const bool full_tile = (n_blk + 1) * kBN <= p.N;
+    int cnt = 0;
+    auto process = [&](const uint32_t(&r)[32], int c) {
+        const int col0 = n_blk * kBN + c * 32;
+        const float *bias = &sh->bias[buf][c * 32];
+        if constexpr (MODE == kDense) {
+            if (full_tile)
+                dense_chunk<OT, JUMP, true>(p, bias, &sh->thr[buf][c * 32], r, row, col0, pol_out, cnt);
+            else
+                dense_chunk<OT, JUMP, false>(p, bias, &sh->thr[buf][c * 32], r, row, col0, pol_out, cnt);
+        } else {
+            topk_chunk(p, bias, r, col0, topk_lists, et, min_key, min_slot);
+        }
+    };
+    // Two register buffers: the load of the next chunk is in flight while one is processed.
+    uint32_t ra[32], rb[32];
+    tmem_ld_32x32b_x32(taddr, ra);
+    tmem_ld_wait();
+#pragma unroll 1
+    for (int c = 0; c < NC; c += 2) {
+        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
+        process(ra, c);
+        tmem_ld_wait();
+        if (c + 2 < NC)
+            tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
+        else
+            release();  // every TMEM read of this tile has completed
+        process(rb, c + 1);
+        if (c + 2 < NC) tmem_ld_wait();
+    }
     if (MODE == kDense && p.row_nnz != nullptr && row < p.M && cnt != 0) atomicAdd(p.row_nnz + row, cnt);
+}
+
+template <int MODE, typename Release>
+__device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
+                                              int et, int row, int n_blk, int buf, uint32_t taddr, uint64_t pol_out,
+                                              unsigned long long &min_key, int &min_slot, Release release) {
+    if (MODE == kTopk) {
+        epilogue_tile_t<kTopk, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
+                                             min_slot, release);
+        return;
+    }
+    const bool jump = p.activation == SF_ACT_JUMPRELU;
+    if (p.out_dtype == SF_BF16) {
+        if (jump)
+            epilogue_tile_t<kDense, __nv_bfloat16, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
+                                                         min_key, min_slot, release);
+        else
+            epilogue_tile_t<kDense, __nv_bfloat16, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
+                                                          min_key, min_slot, release);
+    } else if (p.out_dtype == SF_F16) {
+        if (jump)
+            epilogue_tile_t<kDense, __half, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
+                                                  min_slot, release);
+        else
+            epilogue_tile_t<kDense, __half, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
+                                                   min_slot, release);
+    } else {
+        if (jump)
+            epilogue_tile_t<kDense, float, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
+                                                 min_slot, release);
+        else
+            epilogue_tile_t<kDense, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
+                                                  min_slot, release);
+    }
 }
 
 template <int AB_FMT, bool B_MN, int MODE, int STAGES>
