@@ -123,34 +123,6 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Bounded wait that ignores the abort flag: used only to drain copies in flight.
-__device__ __forceinline__ void mbar_drain(uint64_t *bar, uint32_t parity, unsigned *err) {
-    const uint32_t a = smem_u32(bar);
-    const unsigned long long t0 = global_timer_ns();
-    for (uint32_t i = 0;; ++i) {
-        if (mbar_try_wait(a, parity)) return;
-        if ((i & 31u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(err, kErrTimeout);
-            return;
-        }
-    }
-}
-
-// Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
-__device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int mode, int et, int n_blk, int buf) {
-    for (int j = et; j < kBN; j += 128) {
-        const int col = n_blk * kBN + j;
-        float b = 0.f, t = 0.f;
-        if (col < p.N) {
-            b = load_as_f32(p.b_enc, p.b_enc_dtype, (int64_t)col * p.b_enc_stride);
-            if (mode == kDense && p.activation == SF_ACT_JUMPRELU)
-                t = load_as_f32(p.thr, p.thr_dtype, (int64_t)col * p.thr_stride);
-        }
-        sh->bias[buf][j] = b;
-        sh->thr[buf][j] = t;
-    }
-}
-
 // Packs two fp32 values to the 16-bit output type (round to nearest even); returns the bits.
 template <typename OT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -451,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (*abort_flag) {
                 // Let every copy this thread issued land before shared memory goes away.
                 for (int s = 0; s < STAGES; ++s)
-                    if (armed & (1u << s)) mbar_drain(&sh->full[s], (armed_parity >> s) & 1u, p.err);
+                    if (armed & (1u << s)) mbar_wait_drain(&sh->full[s], (armed_parity >> s) & 1u, p.err);
             }
         }
     } else if (warp == 1) {
@@ -506,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             // Every MMA this thread issued has finished once `drain` completes.
             umma_commit(&sh->drain);
-            mbar_drain(&sh->drain, 0, p.err);
+            mbar_wait_drain(&sh->drain, 0, p.err);
         }
     } else {
         // ---------------------------------------------------------------- epilogue
@@ -674,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (leader) {
                     // Both CTAs' copies of every armed stage complete on these barriers.
                     for (int s = 0; s < STAGES; ++s)
-                        if (armed & (1u << s)) mbar_drain(&sh->full[s], (armed_parity >> s) & 1u, p.err);
+                        if (armed & (1u << s)) mbar_wait_drain(&sh->full[s], (armed_parity >> s) & 1u, p.err);
                 } else {
                     // This CTA's copies complete on the leader's barriers: give them time to land.
                     const unsigned long long t0 = global_timer_ns();
@@ -737,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             umma_commit_pair(map_to_rank(smem_u32(&sh->drain), 0));
-            mbar_drain(&sh->drain, 0, p.err);
+            mbar_wait_drain(&sh->drain, 0, p.err);
         }
     } else {
         // ---------------------------------------------------------------- epilogue (both CTAs)

@@ -130,6 +130,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
+// Bounded wait that ignores the abort flag: used only to let copies in flight land before
+// a kernel that gave up exits.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t *bar, uint32_t parity, unsigned *err_word) {
+    const uint32_t a = smem_u32(bar);
+    const unsigned long long t0 = global_timer_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(a, parity)) return;
+        if ((i & 31u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(err_word, kErrTimeout);
+            return;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------------------
 // TMA (tiled loads into the issuing CTA)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {

@@ -6,6 +6,8 @@
 //   compact_kernel     replaces _compact_kernel         (decode.py:61-74)
 //   decode_kernel      replaces _decode_kernel          (decode.py:28-55)
 //   topk_merge_kernel  replaces torch.topk on the dense ReLU output (saeflow/ops.py:12-16)
+#include <algorithm>
+
 #include "sf_common.cuh"
 #include "sf_internal.h"
 
