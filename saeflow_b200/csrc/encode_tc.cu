@@ -123,6 +123,21 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
+__device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int mode, int et, int n_blk, int buf) {
+    for (int j = et; j < kBN; j += 128) {
+        const int col = n_blk * kBN + j;
+        float b = 0.f, t = 0.f;
+        if (col < p.N) {
+            b = load_as_f32(p.b_enc, p.b_enc_dtype, (int64_t)col * p.b_enc_stride);
+            if (mode == kDense && p.activation == SF_ACT_JUMPRELU)
+                t = load_as_f32(p.thr, p.thr_dtype, (int64_t)col * p.thr_stride);
+        }
+        sh->bias[buf][j] = b;
+        sh->thr[buf][j] = t;
+    }
+}
+
 // Packs two fp32 values to the 16-bit output type (round to nearest even); returns the bits.
 template <typename OT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
