@@ -223,6 +223,7 @@ def l2_flush(buf):
 def run_ours(args, rank, world, device):
     from saeflow_b200 import forward
     from saeflow_b200.kernels import dense_to_csr, device_error, fused_encode, sparse_decode, topk_encode
+    from saeflow_b200.kernels.encode import encode_csr_finish, encode_csr_stage
 
     cfg_id = args.config
     c = CONFIGS[cfg_id]
@@ -253,7 +254,8 @@ def run_ours(args, rank, world, device):
             ev[3].record(stream)
             return out
         launches_per_step = 4  # shift, encode+top-k, merge, decode
-    else:
+    elif args.route == "dense" or cfg_id == 1:
+        # The reference's route: dense features, then compaction (IEEE fp32 always takes it).
         x = make_tokens(cfg_id, rank, device, T)
         row_nnz = torch.zeros(T, dtype=torch.int32, device=device)
 
@@ -270,6 +272,21 @@ def run_ours(args, rank, world, device):
             del f
             return out
         launches_per_step = 5  # shift, encode, indptr scan, compact, decode
+    else:
+        # Encode straight to CSR (what saeflow_b200.encode_sparse runs): no dense features.
+        x = make_tokens(cfg_id, rank, device, T)
+
+        def step(ev):
+            ev[0].record(stream)
+            h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation)
+            ev[1].record(stream)
+            csr = encode_csr_finish(h)
+            ev[2].record(stream)
+            out = sparse_decode(*csr, sae.W_dec, sae.b_dec)
+            ev[3].record(stream)
+            step.nnz = csr[1].numel()
+            return out
+        launches_per_step = 5  # shift, encode+stage, indptr scan, place, decode
 
     def barrier():
         if world > 1:
@@ -364,9 +381,11 @@ def run_ours(args, rank, world, device):
         stages["csr_ms"] = round(mean(csr_ms), 4)
         nnz = step.nnz
         l0 = nnz / T
-        comp_bytes = T * c["d_sae"] * e + nnz * (4 + e) + (T + 1) * 8
-        stages["csr_gbps"] = round(comp_bytes / (mean(csr_ms) / 1e3) / 1e9, 1)
+        if args.route == "dense" or cfg_id == 1:
+            comp_bytes = T * c["d_sae"] * e + nnz * (4 + e) + (T + 1) * 8
+            stages["csr_gbps"] = round(comp_bytes / (mean(csr_ms) / 1e3) / 1e9, 1)
         stages["l0"] = round(l0, 2)
+        stages["route"] = "dense+compaction" if (args.route == "dense" or cfg_id == 1) else "encode straight to CSR"
     elif cfg_id == 3:
         nnz = csr[1].numel()
         l0 = nnz / T
@@ -496,6 +515,8 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--route", choices=["csr", "dense"], default="csr",
+                    help="csr: encode straight to CSR (default); dense: dense features + compaction")
     args = ap.parse_args(argv)
 
     rank = int(os.environ.get("RANK", "0"))

@@ -117,6 +117,38 @@ SF_API int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_
                     const sf_matrix *out, int32_t *row_nnz, int allow_tf32, int variant,
                     void *workspace, size_t workspace_bytes, sf_stream stream);
 
+/* Columns per (row, tile) cell of the encode-straight-to-CSR staging. */
+#define SF_CSR_TILE 256
+
+/*
+ * Encode straight to CSR, step 1: the encoder GEMM without its dense [M, d_sae] output.
+ * For every (row, SF_CSR_TILE-column tile) the epilogue writes the count of stored nonzeros
+ * to tile_counts [M, ceil(d_sae / SF_CSR_TILE)] and, where nonzero, the staging offset of the
+ * tile's (column, value) pairs to tile_offsets; the pairs go to stage_indices / stage_values
+ * (stage_capacity entries, values in values_dtype) in column order; each row's count is added
+ * to row_nnz (caller-zeroed). state[0] (staging cursor) and state[1] (overflow flag) must be
+ * zero on entry; state[1] != 0 afterwards means stage_capacity was too small and the staged
+ * pairs are incomplete. Workspace: sf_fused_encode_workspace. Tensor-core dtypes only
+ * (16-bit W_enc, or fp32 with allow_tf32); IEEE fp32 returns SF_ERR_UNSUPPORTED.
+ * With sf_csr_indptr and sf_csr_place this replaces saeflow/ops.py:36-39 (fused_encode with
+ * row_nnz, then dense_to_csr, decode.py:77-94), producing the identical canonical CSR.
+ */
+SF_API int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
+                               const sf_vector *b_dec, const sf_vector *threshold, int activation,
+                               int values_dtype, int32_t *row_nnz, int32_t *tile_counts, int32_t *tile_offsets,
+                               int32_t *stage_indices, void *stage_values, int64_t stage_capacity, uint32_t *state,
+                               int allow_tf32, void *workspace, size_t workspace_bytes, sf_stream stream);
+
+/*
+ * Encode straight to CSR, step 2 (after sf_csr_indptr on row_nnz and a read of indptr[M] to
+ * size indices / values): moves the staged pairs into canonical CSR order. A cell whose count
+ * or offset is inconsistent (outside [0, SF_CSR_TILE] or the staging capacity) is skipped
+ * and sets bit 4 of the device error.
+ */
+SF_API int sf_csr_place(const int32_t *tile_counts, const int32_t *tile_offsets, int64_t M, int64_t d_sae,
+                        const int32_t *stage_indices, const void *stage_values, int64_t stage_capacity,
+                        int values_dtype, const int64_t *indptr, int32_t *indices, void *values, sf_stream stream);
+
 /*
  * row_nnz[m] = number of f[m, :] != 0 (NaN counts, -0.0 does not). Overwrites.
  * Replaces torch.count_nonzero at saeflow/kernels/decode.py:85.

@@ -23,6 +23,7 @@ SF_VARIANT_AUTO, SF_VARIANT_TCGEN05, SF_VARIANT_SIMT, SF_VARIANT_TCGEN05_SINGLE 
 
 SF_OK, SF_ERR_INVALID, SF_ERR_UNSUPPORTED, SF_ERR_CUDA, SF_ERR_WORKSPACE, SF_ERR_DEVICE = range(6)
 ABI_VERSION = 1
+CSR_TILE = 256  # SF_CSR_TILE
 
 # Every symbol the header declares, with its ctypes signature.
 _c = ctypes
@@ -52,6 +53,9 @@ SIGNATURES = {
     "sf_fused_encode": (_c.c_int, [_MP, _MP, _VP, _VP, _VP, _c.c_int, _MP, _P, _c.c_int, _c.c_int,
                                    _P, _c.c_size_t, _P]),
     "sf_fused_encode_noalloc": (_c.c_int, [_MP, _MP, _VP, _VP, _VP, _c.c_int, _MP, _P, _c.c_int, _c.c_int, _P]),
+    "sf_encode_csr_stage": (_c.c_int, [_MP, _MP, _VP, _VP, _VP, _c.c_int, _c.c_int, _P, _P, _P, _P, _P,
+                                       _c.c_int64, _P, _c.c_int, _P, _c.c_size_t, _P]),
+    "sf_csr_place": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _P, _P, _c.c_int64, _c.c_int, _P, _P, _P, _P]),
     "sf_row_nnz": (_c.c_int, [_MP, _P, _P]),
     "sf_csr_indptr": (_c.c_int, [_P, _c.c_int64, _P, _P]),
     "sf_dense_to_csr": (_c.c_int, [_MP, _P, _P, _P, _c.c_int, _P]),

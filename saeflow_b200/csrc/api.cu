@@ -21,6 +21,9 @@ int launch_decode(const int64_t *indptr, int64_t M, const int32_t *indices, cons
 int launch_topk_merge(const unsigned long long *cand, int64_t M, int ncand, int k, int32_t *out_idx, void *out_val,
                       int vdt, cudaStream_t s);
 int launch_topk_rows(const sf_matrix &f, int k, int32_t *out_idx, void *out_val, int vdt, cudaStream_t s);
+int launch_csr_place(const int32_t *tile_cnt, const int32_t *tile_off, int64_t n_tiles, const int32_t *stage_idx,
+                     const void *stage_val, int64_t stage_cap, int vdt, const int64_t *indptr, int64_t M,
+                     int32_t *indices, void *values, cudaStream_t s);
 
 namespace {
 thread_local char g_last_error[512] = "";
@@ -479,6 +482,90 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
         g.b_pitch = pl.w_pitch;
     }
     return encode_tc_dense(g, ep, variant, s);
+}
+
+int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc, const sf_vector *b_dec,
+                        const sf_vector *threshold, int activation, int values_dtype, int32_t *row_nnz,
+                        int32_t *tile_counts, int32_t *tile_offsets, int32_t *stage_indices, void *stage_values,
+                        int64_t stage_capacity, uint32_t *state, int allow_tf32, void *workspace,
+                        size_t workspace_bytes, sf_stream stream) {
+    int st = check_matrix(x, "x");
+    if (!st) st = check_matrix(W_enc, "W_enc");
+    if (st) return st;
+    const int64_t M = x->rows, K = x->cols, N = W_enc->cols;
+    if (activation != SF_ACT_RELU && activation != SF_ACT_JUMPRELU)
+        return set_error(SF_ERR_INVALID, "unknown activation code %d", activation);
+    if (K != W_enc->rows)
+        return set_error(SF_ERR_INVALID, "x has d_in=%lld but W_enc has d_in=%lld", (long long)K,
+                         (long long)W_enc->rows);
+    if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
+    st = check_vector(b_enc, N, "b_enc", false);
+    if (!st) st = check_vector(b_dec, K, "b_dec", true);
+    if (!st) st = check_vector(threshold, N, "threshold", activation != SF_ACT_JUMPRELU);
+    if (st) return st;
+    if (stage_capacity < 0 || stage_capacity > 2147483647ll)
+        return set_error(SF_ERR_INVALID, "stage_capacity must be in [0, 2^31)");
+    if (M == 0 || N == 0) return SF_OK;
+    if (!tile_counts || !tile_offsets || !state || (stage_capacity > 0 && (!stage_indices || !stage_values)))
+        return set_error(SF_ERR_INVALID, "NULL staging pointer");
+    EncodePlan pl;
+    st = plan_encode(x, W_enc, allow_tf32, SF_VARIANT_AUTO, &pl);
+    if (st) return st;
+    if (!pl.tensor_cores)
+        return set_error(SF_ERR_UNSUPPORTED, "IEEE fp32 encode has no CSR epilogue; use sf_fused_encode");
+    const size_t need = plan_workspace(pl);
+    if (workspace_bytes < need || (!workspace && need))
+        return set_error(SF_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+    if (!aligned16(workspace)) return set_error(SF_ERR_WORKSPACE, "workspace must be 16-byte aligned");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    void *xs = ws;
+    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
+    st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
+    if (st) return st;
+    GemmOperands g{};
+    g.a = xs;
+    g.a_pitch = pl.a_pitch;
+    g.ab_fmt = pl.ab_fmt;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.b_mn_major = pl.b_mn;
+    if (pl.w_direct) {
+        g.b = W_enc->data;
+        g.b_pitch = pl.w_pitch;
+    } else {
+        st = run_repack(W_enc, wp, pl.w_pitch, pl.b_mn, s);
+        if (st) return st;
+        g.b = wp;
+        g.b_pitch = pl.w_pitch;
+    }
+    EpilogueArgs ep{};
+    ep.b_enc = b_enc->data;
+    ep.b_enc_dtype = b_enc->dtype;
+    ep.b_enc_stride = b_enc->stride;
+    if (threshold && threshold->data) {
+        ep.thr = threshold->data;
+        ep.thr_dtype = threshold->dtype;
+        ep.thr_stride = threshold->stride;
+    }
+    ep.activation = activation;
+    ep.out_dtype = values_dtype;
+    ep.row_nnz = row_nnz;
+    CsrArgs csr{tile_counts, tile_offsets, stage_indices, stage_values, state, (unsigned)stage_capacity};
+    return encode_tc_csr(g, ep, csr, s);
+}
+
+int sf_csr_place(const int32_t *tile_counts, const int32_t *tile_offsets, int64_t M, int64_t d_sae,
+                 const int32_t *stage_indices, const void *stage_values, int64_t stage_capacity, int values_dtype,
+                 const int64_t *indptr, int32_t *indices, void *values, sf_stream stream) {
+    if (M < 0 || d_sae < 0 || stage_capacity < 0) return set_error(SF_ERR_INVALID, "negative extent");
+    if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
+    if (M == 0) return SF_OK;
+    if (!tile_counts || !tile_offsets || !indptr) return set_error(SF_ERR_INVALID, "NULL pointer");
+    const int64_t n_tiles = (d_sae + kCsrTile - 1) / kCsrTile;
+    return launch_csr_place(tile_counts, tile_offsets, n_tiles, stage_indices, stage_values, stage_capacity,
+                            values_dtype, indptr, M, indices, values, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int sf_row_nnz(const sf_matrix *f, int32_t *row_nnz, sf_stream stream) {

@@ -50,7 +50,7 @@ constexpr int kTileABytes = kBM * 128;  // 128 rows x 128 B
 constexpr int kTileBBytes = kBN * 128;  // 256 rows (or MN chunks) x 128 B
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
 
-enum Mode { kDense = 0, kTopk = 1 };
+enum Mode { kDense = 0, kTopk = 1, kCsr = 2 };
 
 struct TcParams {
     int M, N, K;
@@ -77,6 +77,13 @@ struct TcParams {
     int k;
     int values_dtype;
     unsigned long long *cand;  // [M, n_chunks, k] packed keys
+    // csr (encode straight to CSR staging)
+    int32_t *tile_cnt;         // [M, num_n_tiles] nonzeros of each (row, n-tile)
+    int32_t *tile_off;         // [M, num_n_tiles] their staging offset (where the count is > 0)
+    int32_t *stage_idx;        // [stage_cap] feature ids
+    void *stage_val;           // [stage_cap] values in out_dtype
+    unsigned *csr_state;       // [0] staging cursor, [1] overflow flag
+    unsigned stage_cap;
 };
 
 struct __align__(8) TcShared {
@@ -98,8 +105,8 @@ struct Unit {
 
 __device__ __forceinline__ Unit unit_coords(const TcParams &p, int u, int mode) {
     Unit r;
-    if (mode == kDense) {
-        // Grouped raster: group_m m-tiles share each W n-tile while it is in L2.
+    if (mode != kTopk) {
+        // One tile per unit, grouped raster: group_m m-tiles share each W n-tile in L2.
         const int per_group = p.group_m * p.num_n_tiles;
         const int g = u / per_group;
         const int first_m = g * p.group_m;
@@ -123,15 +130,30 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity).
+// Largest fp32 value that rounds to zero when stored in `dtype` (round to nearest even):
+// half the smallest subnormal of bf16 (2^-134) and fp16 (2^-25), 0 for fp32.
+__device__ __forceinline__ float zero_cut(int dtype) {
+    if (dtype == SF_BF16) return __uint_as_float(0x00008000u);  // 2^-134 (an fp32 subnormal)
+    if (dtype == SF_F16) return __uint_as_float(0x33000000u);   // 2^-25
+    return 0.f;
+}
+
+// Stage this tile's b_enc / threshold in fp32 (double-buffered by tile parity). In CSR mode
+// the second array holds the cut: a stored value is nonzero exactly when pre > cut, with
+// cut = max(threshold, zero_cut) for JumpReLU (never for a NaN threshold) and zero_cut for
+// ReLU, since v = relu(pre) (or 0 unless pre > threshold) rounds to zero iff v <= zero_cut.
 __device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int mode, int et, int n_blk, int buf) {
+    const float zc = zero_cut(p.out_dtype);
     for (int j = et; j < kBN; j += 128) {
         const int col = n_blk * kBN + j;
         float b = 0.f, t = 0.f;
         if (col < p.N) {
             b = load_as_f32(p.b_enc, p.b_enc_dtype, (int64_t)col * p.b_enc_stride);
-            if (mode == kDense && p.activation == SF_ACT_JUMPRELU)
+            if (mode != kTopk && p.activation == SF_ACT_JUMPRELU)
                 t = load_as_f32(p.thr, p.thr_dtype, (int64_t)col * p.thr_stride);
+            if (mode == kCsr) t = p.activation == SF_ACT_JUMPRELU ? (t != t ? __int_as_float(0x7f800000) : fmaxf(t, zc)) : zc;
+        } else if (mode == kCsr) {
+            t = __int_as_float(0x7f800000);  // +inf: columns past d_sae never fire
         }
         sh->bias[buf][j] = b;
         sh->thr[buf][j] = t;
@@ -272,6 +294,102 @@ __device__ __forceinline__ void topk_chunk(const TcParams &p, const float *bias,
     }
 }
 
+// CSR pass 1 of one 32-column chunk: bit j of the returned mask is set when column col0+j
+// stores a nonzero value, i.e. when pre = acc + b_enc exceeds the staged cut (which is +inf
+// past d_sae).
+__device__ __forceinline__ uint32_t csr_chunk_mask(const float *bias, const float *cut, const uint32_t (&r)[32]) {
+    uint32_t m = 0;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 b4 = *reinterpret_cast<const float4 *>(bias + j);
+        const float4 c4 = *reinterpret_cast<const float4 *>(cut + j);
+        m |= (__uint_as_float(r[j + 0]) + b4.x > c4.x ? 1u : 0u) << (j + 0);
+        m |= (__uint_as_float(r[j + 1]) + b4.y > c4.y ? 1u : 0u) << (j + 1);
+        m |= (__uint_as_float(r[j + 2]) + b4.z > c4.z ? 1u : 0u) << (j + 2);
+        m |= (__uint_as_float(r[j + 3]) + b4.w > c4.w ? 1u : 0u) << (j + 3);
+    }
+    return m;
+}
+
+// CSR pass 2 of one chunk: writes the (column, value) pairs of the set bits of `m` to the
+// staging arrays from `o` on, in column order. A set bit means pre > threshold, so the
+// stored value is relu(pre) rounded to OT.
+template <typename OT>
+__device__ __forceinline__ void csr_chunk_emit(const TcParams &p, const float *bias, const uint32_t (&r)[32],
+                                               int col0, uint32_t m, unsigned &o) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        if (m & (1u << j)) {
+            const float v = fmaxf(__uint_as_float(r[j]) + bias[j], 0.f);
+            p.stage_idx[o] = col0 + j;
+            reinterpret_cast<OT *>(p.stage_val)[o] = from_f32<OT>(v);
+            ++o;
+        }
+    }
+}
+
+// CSR epilogue of one tile: pass 1 over all chunks finds each row's nonzeros, one atomicAdd
+// per warp reserves staging space for the warp's 32 rows, pass 2 re-reads from TMEM only the
+// chunks where some row of the warp has a nonzero and emits them.
+template <typename OT, typename Release>
+__device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, int row, int n_blk, int buf,
+                                         uint32_t taddr, Release release) {
+    constexpr int NC = kBN / 32;
+    const bool live = row < p.M;
+    uint32_t masks[NC];
+    int cnt = 0;
+    uint32_t ra[32], rb[32];
+    tmem_ld_32x32b_x32(taddr, ra);
+    tmem_ld_wait();
+#pragma unroll
+    for (int c = 0; c < NC; c += 2) {
+        tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
+        masks[c] = csr_chunk_mask(&sh->bias[buf][c * 32], &sh->thr[buf][c * 32], ra);
+        tmem_ld_wait();
+        if (c + 2 < NC) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
+        masks[c + 1] = csr_chunk_mask(&sh->bias[buf][(c + 1) * 32], &sh->thr[buf][(c + 1) * 32], rb);
+        if (c + 2 < NC) tmem_ld_wait();
+    }
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+        if (!live) masks[c] = 0;
+        cnt += __popc(masks[c]);
+    }
+    // Reserve staging space for the warp's rows with one atomic.
+    const int lane = (int)lane_id();
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += t;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    unsigned base = 0;
+    if (lane == 31 && total > 0) base = atomicAdd(&p.csr_state[0], (unsigned)total);
+    base = __shfl_sync(0xffffffffu, base, 31);
+    unsigned o = base + (unsigned)(incl - cnt);
+    const bool fits = (unsigned long long)base + (unsigned long long)total <= (unsigned long long)p.stage_cap;
+    if (lane == 31 && total > 0 && !fits) atomicOr(&p.csr_state[1], 1u);
+    if (live) {
+        const int64_t cell = (int64_t)row * p.num_n_tiles + n_blk;
+        p.tile_cnt[cell] = cnt;
+        if (cnt) p.tile_off[cell] = (int)o;
+        if (p.row_nnz != nullptr && cnt) atomicAdd(p.row_nnz + row, cnt);
+    }
+    if (fits) {
+#pragma unroll 1
+        for (int c = 0; c < NC; ++c) {
+            if (__any_sync(0xffffffffu, masks[c] != 0)) {
+                uint32_t rr[32];
+                tmem_ld_32x32b_x32(taddr + c * 32, rr);
+                tmem_ld_wait();
+                if (masks[c]) csr_chunk_emit<OT>(p, &sh->bias[buf][c * 32], rr, n_blk * kBN + c * 32, masks[c], o);
+            }
+        }
+    }
+    release();  // all TMEM reads of this tile have completed
+}
+
 // One tile of epilogue for this thread's row: reads the 256 fp32 accumulators of its TMEM
 // lane 32 columns at a time, loading chunk c+1 while chunk c is processed; `release` runs
 // once all TMEM reads of the tile are complete, so the MMA warp may reuse the buffer.
@@ -318,7 +436,16 @@ template <int MODE, typename Release>
 __device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
                                               int et, int row, int n_blk, int buf, uint32_t taddr, uint64_t pol_out,
                                               unsigned long long &min_key, int &min_slot, Release release) {
-    if (MODE == kTopk) {
+    if constexpr (MODE == kCsr) {
+        if (p.out_dtype == SF_BF16)
+            csr_tile<__nv_bfloat16>(p, sh, row, n_blk, buf, taddr, release);
+        else if (p.out_dtype == SF_F16)
+            csr_tile<__half>(p, sh, row, n_blk, buf, taddr, release);
+        else
+            csr_tile<float>(p, sh, row, n_blk, buf, taddr, release);
+        return;
+    }
+    if constexpr (MODE == kTopk) {
         epilogue_tile_t<kTopk, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
                                              min_slot, release);
         return;
@@ -953,6 +1080,38 @@ int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, 
     p.row_nnz = ep.row_nnz;
     if (pair) return dispatch<kDense, 6, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
     return dispatch<kDense, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
+}
+
+int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &csr, cudaStream_t stream) {
+    const bool pair = g.M > kBM;
+    CUtensorMap tmA, tmB;
+    int st = build_maps(g, pair, &tmA, &tmB);
+    if (st) return st;
+    TcParams p{};
+    fill_common(p, g, pair, device_error_word());
+    const int es = g.ab_fmt == 2 ? 4 : 2;
+    const int64_t a_tile_bytes = (int64_t)p.bm * g.K * es;
+    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, (64ll << 20) / std::max<int64_t>(1, a_tile_bytes)));
+    p.num_units = p.num_m_tiles * p.num_n_tiles;
+    p.n_chunks = 1;
+    p.tiles_per_chunk = 1;
+    p.b_enc = ep.b_enc;
+    p.b_enc_dtype = ep.b_enc_dtype;
+    p.b_enc_stride = ep.b_enc_stride;
+    p.thr = ep.thr;
+    p.thr_dtype = ep.thr_dtype;
+    p.thr_stride = ep.thr_stride;
+    p.activation = ep.activation;
+    p.out_dtype = ep.out_dtype;
+    p.row_nnz = ep.row_nnz;
+    p.tile_cnt = csr.tile_cnt;
+    p.tile_off = csr.tile_off;
+    p.stage_idx = csr.stage_idx;
+    p.stage_val = csr.stage_val;
+    p.csr_state = csr.state;
+    p.stage_cap = csr.cap;
+    if (pair) return dispatch<kCsr, 6, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
+    return dispatch<kCsr, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
 }
 
 // Column chunks per row for the top-k schedule: enough (m-tile, chunk) units to fill the

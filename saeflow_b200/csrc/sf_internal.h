@@ -46,7 +46,19 @@ struct TopkArgs {
     unsigned long long *cand;  // [M, n_chunks, k]
 };
 
+// Staging of the encode-straight-to-CSR path.
+struct CsrArgs {
+    int32_t *tile_cnt;   // [M, n_tiles]
+    int32_t *tile_off;   // [M, n_tiles]
+    int32_t *stage_idx;  // [cap]
+    void *stage_val;     // [cap]
+    unsigned *state;     // [0] cursor, [1] overflow
+    unsigned cap;
+};
+constexpr int kCsrTile = 256;  // columns per (row, tile) count cell
+
 int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, cudaStream_t stream);
+int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &csr, cudaStream_t stream);
 int pair_slots(const void *kern, const cudaLaunchConfig_t &cfg);
 int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t stream);
 int topk_chunks(int64_t M, int64_t N);

@@ -390,6 +390,47 @@ __global__ void __launch_bounds__(128) decode_generic_kernel(const int64_t *__re
     }
 }
 
+// ------------------------------------------------------------------ CSR placement
+// Moves the staged (column, value) pairs of the encode-straight-to-CSR path into canonical
+// CSR: one warp per row scans the row's per-tile counts (tiles in column order) to find
+// each tile's output slot and copies the tile's staged run there.
+template <typename VT>
+__global__ void csr_place_kernel(const int32_t *__restrict__ tile_cnt, const int32_t *__restrict__ tile_off,
+                                 int64_t n_tiles, const int32_t *__restrict__ stage_idx,
+                                 const VT *__restrict__ stage_val, int64_t stage_cap,
+                                 const int64_t *__restrict__ indptr, int64_t M, int32_t *__restrict__ indices,
+                                 VT *__restrict__ values, unsigned *err) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= M) return;
+    const int lane = lane_id();
+    const int64_t start = indptr[row], end = indptr[row + 1];
+    int64_t run = start;
+    bool bad = false;
+    for (int64_t t0 = 0; t0 < n_tiles; t0 += 32) {
+        const int64_t t = t0 + lane;
+        int c = t < n_tiles ? tile_cnt[row * n_tiles + t] : 0;
+        if (c < 0 || c > kCsrTile) {  // a cell the encoder did not write: report, never follow
+            bad = true;
+            c = 0;
+        }
+        const int incl = warp_inclusive_scan(c);
+        if (c > 0) {
+            const int64_t dst = run + incl - c;
+            const int64_t src = tile_off[row * n_tiles + t];
+            if (dst + c > end || src < 0 || src + c > stage_cap) {
+                bad = true;
+            } else {
+                for (int j = 0; j < c; ++j) {
+                    indices[dst + j] = stage_idx[src + j];
+                    values[dst + j] = stage_val[src + j];
+                }
+            }
+        }
+        run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (__any_sync(0xffffffffu, bad || run != end) && lane == 0) atomicOr(err, kErrIndptr);
+}
+
 // ------------------------------------------------------------------ top-k merge
 // One warp per row: k rounds of a warp-wide max over the row's n_chunks*k packed
 // (value, ~index) keys; the winner is removed from its lane's registers... kept in
@@ -654,6 +695,21 @@ int launch_topk_rows(const sf_matrix &f, int k, int32_t *out_idx, void *out_val,
                                                      out_idx, reinterpret_cast<VT *>(out_val));
             return check_cuda(cudaGetLastError(), "topk rows launch");
         });
+    });
+}
+}  // namespace sf
+
+namespace sf {
+int launch_csr_place(const int32_t *tile_cnt, const int32_t *tile_off, int64_t n_tiles, const int32_t *stage_idx,
+                     const void *stage_val, int64_t stage_cap, int vdt, const int64_t *indptr, int64_t M,
+                     int32_t *indices, void *values, cudaStream_t s) {
+    if (M == 0) return SF_OK;
+    return by_dtype(vdt, [&](auto tag) {
+        using VT = decltype(tag);
+        csr_place_kernel<VT><<<(unsigned)((M + 7) / 8), 256, 0, s>>>(
+            tile_cnt, tile_off, n_tiles, stage_idx, reinterpret_cast<const VT *>(stage_val), stage_cap, indptr, M,
+            indices, reinterpret_cast<VT *>(values), device_error_word());
+        return check_cuda(cudaGetLastError(), "csr place launch");
     });
 }
 }  // namespace sf

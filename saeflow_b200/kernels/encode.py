@@ -114,3 +114,106 @@ def best_config():
     The reference returns the autotuner's pick (encode.py:142-144); these kernels have
     one tile shape each, so this names the kernel that ran."""
     return _last_config
+
+
+def encode_csr(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *, allow_tf32=None,
+               stage_capacity=None):
+    """CSR features (indptr int64 [M+1], indices int32 [nnz], values [nnz]) of
+    act((x - b_dec) @ W_enc + b_enc), without the dense [M, d_sae] output.
+
+    Returns exactly `dense_to_csr(fused_encode(..., row_nnz=r), r)` (the reference's
+    encode_sparse, saeflow/ops.py:36-39): the GEMM epilogue stages each row's nonzeros per
+    256-column tile and a placement kernel writes the canonical CSR after the one host sync
+    that sizes it. IEEE fp32 (no tensor cores) and a staging overflow (more nonzeros than
+    `stage_capacity`, default min(d_sae, 512) per row) take the dense route instead.
+    """
+    staged = encode_csr_stage(x, W_enc, b_enc, b_dec, threshold, activation, allow_tf32=allow_tf32,
+                              stage_capacity=stage_capacity)
+    return encode_csr_finish(staged)
+
+
+class _Staged:
+    """Device buffers of an encode-straight-to-CSR call between its two steps."""
+
+    __slots__ = ("args", "dev", "M", "N", "dtype", "row_nnz", "tile_cnt", "tile_off", "stage_idx", "stage_val",
+                 "state", "csr")
+
+
+def encode_csr_stage(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *, allow_tf32=None,
+                     stage_capacity=None):
+    """Step 1 of encode_csr: launches the shift pre-pass and the encoder GEMM with the CSR
+    staging epilogue (no host sync). Pass the result to encode_csr_finish."""
+    if activation not in ACTIVATIONS:
+        raise ValueError(f"fused_encode supports {list(ACTIVATIONS)}, got {activation!r}")
+    if activation == "jumprelu" and threshold is None:
+        raise ValueError("jumprelu needs a threshold")
+    M, K = x.shape
+    K_w, N = W_enc.shape
+    if K != K_w:
+        raise ValueError(f"x has d_in={K} but W_enc has d_in={K_w}")
+    dev = _abi.require_cuda(("x", x), ("W_enc", W_enc), ("b_enc", b_enc), ("b_dec", b_dec),
+                            ("threshold", threshold))
+    if allow_tf32 is None:
+        allow_tf32 = torch.backends.cuda.matmul.allow_tf32
+    h = _Staged()
+    h.args = (x, W_enc, b_enc, b_dec, threshold, activation, allow_tf32)
+    h.dev, h.M, h.N, h.dtype, h.csr = dev, M, N, x.dtype, None
+    if M == 0 or not _uses_tensor_cores(x, W_enc, allow_tf32, _abi.SF_VARIANT_AUTO):
+        h.csr = _dense_route(h)
+        return h
+    n_tiles = (N + _abi.CSR_TILE - 1) // _abi.CSR_TILE
+    cap = stage_capacity if stage_capacity is not None else M * min(N, 512)
+    cap = int(max(0, min(cap, (1 << 31) - 1)))
+    lib = _abi.load()
+    xm, wm = _abi.matrix(x, "x"), _abi.matrix(W_enc, "W_enc")
+    be, bd = _abi.vector(b_enc, "b_enc"), _abi.vector(b_dec, "b_dec")
+    th = _abi.vector(threshold, "threshold") if activation == "jumprelu" else None
+    with torch.cuda.device(dev):
+        h.row_nnz = torch.zeros(M, dtype=torch.int32, device=dev)
+        h.tile_cnt = torch.empty(M * n_tiles, dtype=torch.int32, device=dev)
+        h.tile_off = torch.empty(M * n_tiles, dtype=torch.int32, device=dev)
+        h.stage_idx = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
+        h.stage_val = torch.empty(max(cap, 1), dtype=x.dtype, device=dev)
+        h.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        need = ctypes.c_size_t(0)
+        _abi.check(lib.sf_fused_encode_workspace(ctypes.byref(xm), ctypes.byref(wm), int(bool(allow_tf32)),
+                                                 _abi.SF_VARIANT_AUTO, ctypes.byref(need)))
+        ws = torch.empty(max(need.value, 16), dtype=torch.uint8, device=dev)
+        _abi.check(lib.sf_encode_csr_stage(
+            ctypes.byref(xm), ctypes.byref(wm), _abi.ref(be), _abi.ref(bd), _abi.ref(th), ACTIVATIONS[activation],
+            _abi.dtype_code(x.dtype, "x"), h.row_nnz.data_ptr(), h.tile_cnt.data_ptr(), h.tile_off.data_ptr(),
+            h.stage_idx.data_ptr(), h.stage_val.data_ptr(), cap, h.state.data_ptr(), int(bool(allow_tf32)),
+            ws.data_ptr(), ws.numel(), _abi.stream_of(dev)))
+    return h
+
+
+def encode_csr_finish(h):
+    """Step 2 of encode_csr: indptr scan, the one host sync (nnz and the overflow flag),
+    and the placement kernel. Returns (indptr, indices, values)."""
+    if h.csr is not None:
+        return h.csr
+    lib = _abi.load()
+    M, N, dev = h.M, h.N, h.dev
+    with torch.cuda.device(dev):
+        s = _abi.stream_of(dev)
+        indptr = torch.empty(M + 1, dtype=torch.int64, device=dev)
+        _abi.check(lib.sf_csr_indptr(h.row_nnz.data_ptr(), M, indptr.data_ptr(), s))
+        nnz, overflow = torch.stack([indptr[-1], h.state[1].to(torch.int64)]).tolist()  # the one host sync
+        if overflow:
+            return _dense_route(h)
+        indices = torch.empty(nnz, dtype=torch.int32, device=dev)
+        values = torch.empty(nnz, dtype=h.dtype, device=dev)
+        if nnz:
+            _abi.check(lib.sf_csr_place(h.tile_cnt.data_ptr(), h.tile_off.data_ptr(), M, N, h.stage_idx.data_ptr(),
+                                        h.stage_val.data_ptr(), h.stage_idx.numel(), _abi.dtype_code(h.dtype, "values"),
+                                        indptr.data_ptr(), indices.data_ptr(), values.data_ptr(), s))
+    return indptr, indices, values
+
+
+def _dense_route(h):
+    from .decode import dense_to_csr
+
+    x, W_enc, b_enc, b_dec, threshold, activation, allow_tf32 = h.args
+    rn = torch.zeros(h.M, dtype=torch.int32, device=h.dev)
+    f = fused_encode(x, W_enc, b_enc, b_dec, threshold, activation, row_nnz=rn, allow_tf32=allow_tf32)
+    return dense_to_csr(f, rn)

@@ -7,7 +7,7 @@ Sparse features are CSR tuples (indptr, indices, values); see kernels/decode.py.
 
 import torch
 
-from .kernels import dense_to_csr, fused_encode, sparse_decode, topk_encode
+from .kernels import encode_csr, fused_encode, sparse_decode, topk_encode
 
 
 def _topk(sae, x):
@@ -37,9 +37,9 @@ def encode_sparse(sae, x):
         values, indices = _topk(sae, x)
         indptr = torch.arange(0, M * sae.k + 1, sae.k, device=x.device, dtype=torch.int64)
         return indptr, indices.flatten(), values.flatten()
-    row_nnz = torch.zeros(M, device=x.device, dtype=torch.int32)
-    f = fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation, row_nnz=row_nnz)
-    return dense_to_csr(f, row_nnz)
+    # Same CSR as fused_encode(row_nnz=...) + dense_to_csr (ops.py:37-39), built from the
+    # encoder's epilogue without writing or re-reading the dense [M, d_sae] features.
+    return encode_csr(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation)
 
 
 def decode_sparse(sae, csr):

@@ -11,7 +11,8 @@ import torch
 import oracle
 import saeflow_b200
 from golden_io import Golden
-from saeflow_b200.kernels import csr_to_dense, dense_to_csr, device_error, fused_encode, sparse_decode, topk_encode
+from saeflow_b200.kernels import (csr_to_dense, dense_to_csr, device_error, encode_csr, fused_encode,
+                                  sparse_decode, topk_encode)
 
 pytestmark = pytest.mark.gpu
 
@@ -212,6 +213,84 @@ def test_dense_to_csr_given_row_nnz_matches_counted():
     b = dense_to_csr(f)
     for u, v in zip(a, b):
         assert torch.equal(u, v)
+
+
+# ----------------------------------------------------------------------------- encode straight to CSR
+
+def _assert_same_csr(a, b):
+    for u, v in zip(a, b):
+        assert u.dtype == v.dtype and u.shape == v.shape
+        bits = (lambda t: t.view(torch.int16)) if v.element_size() == 2 and v.is_floating_point() else (lambda t: t)
+        assert torch.equal(bits(u), bits(v))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("activation", ["relu", "jumprelu"])
+@pytest.mark.parametrize("shape", [(1, 16, 32), (37, 50, 129), (300, 128, 1000), (700, 256, 4099), (2000, 512, 8192)])
+def test_encode_csr_identical_to_dense_route(dtype, activation, shape):
+    """Encode straight to CSR gives bit-for-bit the CSR of fused_encode + dense_to_csr."""
+    M, d_in, d_sae = shape
+    sae = make_sae(d_in, d_sae, activation, dtype).to("cuda")
+    if activation == "relu":
+        sae.b_enc.sub_(1.0)  # sparse features
+    x = torch.randn(M, d_in, device="cuda").to(dtype)
+    rn = torch.zeros(M, device="cuda", dtype=torch.int32)
+    want = dense_to_csr(fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, activation, row_nnz=rn), rn)
+    got = encode_csr(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, activation)
+    _assert_same_csr(got, want)
+
+
+def test_encode_csr_dense_rows_and_overflow_fallback():
+    """A fully active row, an all-zero row, and a staging capacity too small: the overflow
+    is detected and the dense route returns the same CSR."""
+    sae = make_sae(64, 600, "relu", torch.bfloat16).to("cuda")
+    x = torch.randn(200, 64, device="cuda").to(torch.bfloat16)
+    x[3] = 0
+    sae.b_enc[:] = -5.0
+    sae.b_enc[:300] = 5.0  # every row has >= 300 active features
+    rn = torch.zeros(200, device="cuda", dtype=torch.int32)
+    want = dense_to_csr(fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, row_nnz=rn), rn)
+    _assert_same_csr(encode_csr(x, sae.W_enc, sae.b_enc, sae.b_dec), want)
+    _assert_same_csr(encode_csr(x, sae.W_enc, sae.b_enc, sae.b_dec, stage_capacity=1000), want)
+    _assert_same_csr(encode_csr(x, sae.W_enc, sae.b_enc, sae.b_dec, stage_capacity=0), want)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_encode_csr_values_that_round_to_zero(dtype):
+    """Pre-activations just above / at / below half the smallest subnormal of the output
+    type: the CSR route keeps exactly the values the dense route stores as nonzero."""
+    d_in, d_sae, M = 16, 512, 130
+    half_min = 2.0 ** -134 if dtype == torch.bfloat16 else 2.0 ** -25
+    x = torch.zeros(M, d_in, device="cuda", dtype=dtype)
+    W = torch.zeros(d_in, d_sae, device="cuda", dtype=dtype)
+    # x = 0 and W = 0 make pre = b_enc exactly; b_enc is fp32 so it can hold the boundary values
+    b_enc = torch.zeros(d_sae, device="cuda", dtype=torch.float32)
+    vals = torch.tensor([half_min * f for f in (0.5, 0.999, 1.0, 1.001, 1.5, 2.0, 4.0)], dtype=torch.float64)
+    b_enc[: vals.numel()] = vals.to(torch.float32).cuda()
+    b_enc[100] = 1.0
+    b_dec = torch.zeros(d_in, device="cuda", dtype=dtype)
+    thr = torch.full((d_sae,), -1.0, device="cuda")
+    thr[101] = float("nan")
+    b_enc[101] = 1.0
+    for act in ("relu", "jumprelu"):
+        rn = torch.zeros(M, device="cuda", dtype=torch.int32)
+        want = dense_to_csr(fused_encode(x, W, b_enc, b_dec, thr, act, row_nnz=rn), rn)
+        got = encode_csr(x, W, b_enc, b_dec, thr, act)
+        _assert_same_csr(got, want)
+    assert int(want[1].numel()) > 0
+
+
+def test_encode_csr_strided_inputs_and_empty():
+    sae = make_sae(96, 513, "jumprelu", torch.bfloat16).to("cuda")
+    xb = torch.randn(90, 100, device="cuda").to(torch.bfloat16)
+    x = xb[:, 2:98]
+    W = sae.W_enc.T.contiguous().T
+    rn = torch.zeros(90, device="cuda", dtype=torch.int32)
+    want = dense_to_csr(fused_encode(x, W, sae.b_enc, sae.b_dec, sae.threshold, "jumprelu", row_nnz=rn), rn)
+    _assert_same_csr(encode_csr(x, W, sae.b_enc, sae.b_dec, sae.threshold, "jumprelu"), want)
+    ip, ix, vs = encode_csr(torch.empty(0, 96, device="cuda", dtype=torch.bfloat16), W, sae.b_enc, sae.b_dec,
+                            sae.threshold, "jumprelu")
+    assert ip.tolist() == [0] and ix.numel() == 0 and vs.numel() == 0
 
 
 # ----------------------------------------------------------------------------- decode
