@@ -58,6 +58,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     headers = _headers()
     cc = nvcc()
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+    extra += os.environ.get("SAEFLOW_B200_NVCC_FLAGS", "").split()  # e.g. -DSF_RASTER_GROUP_MB=32
 
     def compile_one(src: Path) -> Path:
         obj = BUILD / (src.stem + ".o")

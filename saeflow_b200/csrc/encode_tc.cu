@@ -52,6 +52,13 @@ constexpr int kStageBytes = kTileABytes + kTileBBytes;
 
 enum Mode { kDense = 0, kTopk = 1, kCsr = 2 };
 
+// Bytes of x a raster group of m-tiles may span: the group's m-tiles run side by side over
+// each W_enc n-tile, so W_enc is read from HBM once per group while the group's x stays in L2.
+#ifndef SF_RASTER_GROUP_MB
+#define SF_RASTER_GROUP_MB 32
+#endif
+constexpr long long kRasterGroupBytes = (long long)SF_RASTER_GROUP_MB << 20;
+
 struct TcParams {
     int M, N, K;
     int bm;               // rows per tile: 128 (single CTA) or 256 (CTA pair)
@@ -1061,7 +1068,7 @@ int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, 
     // x (A) stays L2-resident when a group of m-tiles fits in ~64 MB.
     const int es = g.ab_fmt == 2 ? 4 : 2;
     const int64_t a_tile_bytes = (int64_t)p.bm * g.K * es;
-    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, (64ll << 20) / std::max<int64_t>(1, a_tile_bytes)));
+    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, kRasterGroupBytes / std::max<int64_t>(1, a_tile_bytes)));
     p.num_units = p.num_m_tiles * p.num_n_tiles;
     p.n_chunks = 1;
     p.tiles_per_chunk = 1;
@@ -1091,7 +1098,7 @@ int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &
     fill_common(p, g, pair, device_error_word());
     const int es = g.ab_fmt == 2 ? 4 : 2;
     const int64_t a_tile_bytes = (int64_t)p.bm * g.K * es;
-    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, (64ll << 20) / std::max<int64_t>(1, a_tile_bytes)));
+    p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, kRasterGroupBytes / std::max<int64_t>(1, a_tile_bytes)));
     p.num_units = p.num_m_tiles * p.num_n_tiles;
     p.n_chunks = 1;
     p.tiles_per_chunk = 1;
