@@ -44,7 +44,13 @@ CONFIGS = {
             dtype=torch.bfloat16, tokens=65536, l0=64.0),
     4: dict(name="cfg4 TopK k=32 bf16 d_in=4096 d_sae=131072", activation="topk", d_in=4096, d_sae=131072,
             dtype=torch.bfloat16, tokens=32768, k=32),
+    # tokens = the whole job's batch, split over the ranks (token partition) or run on every
+    # rank against its feature slice (feature partition): strong scaling.
+    5: dict(name="cfg5 JumpReLU bf16 d_in=2304 d_sae=1048576", activation="jumprelu", d_in=2304, d_sae=1048576,
+            dtype=torch.bfloat16, tokens=262144, l0=96.0),
 }
+CFG5_FEATURE_BLOCK = 65536  # config 5 weights are drawn per block of features (any rank count gets the same W)
+TOKEN_CHUNK = 16384  # config 5 tokens are drawn per chunk of rows
 
 
 # ------------------------------------------------------------------------------ inputs
@@ -104,6 +110,51 @@ def make_sae(cfg_id, device, seed=0):
         p = zipf_probs(c["d_sae"], c["l0"], gen, device)
         sae.threshold = torch.nn.Parameter(normal_isf(p).float().to(dt), requires_grad=False)
     return sae
+
+
+def make_sae_cfg5(device, start, stop, seed=0):
+    """Config 5 weights restricted to features [start, stop). W_dec rows are drawn per block
+    of CFG5_FEATURE_BLOCK features from a generator seeded by the block id, and the threshold
+    permutation over all d_sae features from one generator, so every rank count and every
+    feature slice sees the same SAE."""
+    from saeflow_b200 import SAE
+
+    c = CONFIGS[5]
+    dt, d_in, d_sae = c["dtype"], c["d_in"], c["d_sae"]
+    sae = SAE.__new__(SAE)
+    torch.nn.Module.__init__(sae)
+    sae.d_in, sae.d_sae, sae.activation, sae.k = d_in, stop - start, "jumprelu", None
+    W_dec = torch.empty(stop - start, d_in, dtype=dt, device=device)
+    for b0 in range(start - start % CFG5_FEATURE_BLOCK, stop, CFG5_FEATURE_BLOCK):
+        gen = torch.Generator(device=device).manual_seed(seed * 7919 + 5_000_011 + b0 // CFG5_FEATURE_BLOCK)
+        blk = unit_rows(CFG5_FEATURE_BLOCK, d_in, gen, device)
+        lo, hi = max(start, b0), min(stop, b0 + CFG5_FEATURE_BLOCK)
+        W_dec[lo - start:hi - start] = blk[lo - b0:hi - b0].to(dt)
+        del blk
+    sae.W_dec = torch.nn.Parameter(W_dec, requires_grad=False)
+    sae.W_enc = torch.nn.Parameter(W_dec.T.contiguous(), requires_grad=False)
+    gen = torch.Generator(device=device).manual_seed(seed * 7919 + 5_000_003)
+    sae.b_enc = torch.nn.Parameter(torch.zeros(stop - start, device=device, dtype=dt), requires_grad=False)
+    sae.b_dec = torch.nn.Parameter((torch.randn(d_in, generator=gen, device=device) * 0.1).to(dt),
+                                   requires_grad=False)
+    p = zipf_probs(d_sae, c["l0"], gen, device)[start:stop]
+    sae.threshold = torch.nn.Parameter(normal_isf(p).float().to(dt), requires_grad=False)
+    sae.feature_start = start
+    return sae
+
+
+def make_token_range(cfg_id, t0, t1, device):
+    """Rows [t0, t1) of a config's token stream, drawn per TOKEN_CHUNK rows from a generator
+    seeded by the chunk id (the same rows at any rank count)."""
+    c = CONFIGS[cfg_id]
+    out = torch.empty(t1 - t0, c["d_in"], dtype=c["dtype"], device=device)
+    for ch in range(t0 // TOKEN_CHUNK, (t1 + TOKEN_CHUNK - 1) // TOKEN_CHUNK):
+        c0 = ch * TOKEN_CHUNK
+        gen = torch.Generator(device=device).manual_seed(1_000_003 + 131 * cfg_id + ch)
+        rows = torch.randn(TOKEN_CHUNK, c["d_in"], generator=gen, device=device)
+        lo, hi = max(t0, c0), min(t1, c0 + TOKEN_CHUNK)
+        out[lo - t0:hi - t0] = rows[lo - c0:hi - c0].to(c["dtype"])
+    return out
 
 
 def make_tokens(cfg_id, chunk, device, tokens=None):
@@ -228,11 +279,37 @@ def run_ours(args, rank, world, device):
     cfg_id = args.config
     c = CONFIGS[cfg_id]
     T = args.tokens or c["tokens"]
-    sae = make_sae(cfg_id, device)
+    job_tokens = world * T  # tokens the whole job processes per step (weak scaling)
+    sharded = None
+    if cfg_id == 5:
+        from saeflow_b200.sharded import FeatureShardedSAE, shard_range
+
+        job_tokens = T  # strong scaling: the job's batch is fixed
+        if args.partition == "feature":
+            f0, f1 = shard_range(c["d_sae"], world, rank)
+            sae = make_sae_cfg5(device, f0, f1)
+            x = make_token_range(5, 0, T, device)
+            sharded = FeatureShardedSAE(sae, chunk_tokens=args.chunk_tokens)
+        else:
+            t0, t1 = shard_range(T, world, rank)
+            sae = make_sae_cfg5(device, 0, c["d_sae"])
+            x = make_token_range(5, t0, t1, device)
+            T = t1 - t0
+    else:
+        sae = make_sae(cfg_id, device)
     flush = torch.zeros(64 << 20, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
 
-    if cfg_id == 3:
+    if sharded is not None:
+        n_chunks = (T + args.chunk_tokens - 1) // args.chunk_tokens
+
+        def step(ev):
+            ev[0].record(stream)
+            out = sharded.forward(x)
+            ev[3].record(stream)
+            return out
+        launches_per_step = 5 * n_chunks  # per token chunk: shift, encode+stage, indptr scan, place, decode
+    elif cfg_id == 3:
         csr = make_csr(cfg_id, rank, device, T)
 
         def step(ev):
@@ -274,7 +351,8 @@ def run_ours(args, rank, world, device):
         launches_per_step = 5  # shift, encode, indptr scan, compact, decode
     else:
         # Encode straight to CSR (what saeflow_b200.encode_sparse runs): no dense features.
-        x = make_tokens(cfg_id, rank, device, T)
+        if cfg_id != 5:
+            x = make_tokens(cfg_id, rank, device, T)
 
         def step(ev):
             ev[0].record(stream)
@@ -307,9 +385,10 @@ def run_ours(args, rank, world, device):
         barrier()
         wall = time.perf_counter() - wall0
     step_ms = [e[0].elapsed_time(e[3]) for e in events]
-    enc_ms = [e[0].elapsed_time(e[1]) for e in events] if cfg_id != 3 else []
-    csr_ms = [e[1].elapsed_time(e[2]) for e in events] if cfg_id in (1, 2) else []
-    dec_ms = [e[2].elapsed_time(e[3]) for e in events] if cfg_id != 3 else step_ms
+    staged = cfg_id != 3 and sharded is None  # stage events recorded
+    enc_ms = [e[0].elapsed_time(e[1]) for e in events] if staged else []
+    csr_ms = [e[1].elapsed_time(e[2]) for e in events] if cfg_id in (1, 2, 5) and staged else []
+    dec_ms = [e[2].elapsed_time(e[3]) for e in events] if staged else (step_ms if cfg_id == 3 else [])
     total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)
@@ -317,7 +396,7 @@ def run_ours(args, rank, world, device):
 
     # ---- end to end through the public API with host buffers (H2D in, D2H out, per step)
     e2e = None
-    if cfg_id in (1, 2, 4) and not args.no_e2e:
+    if cfg_id in (1, 2, 4, 5) and not args.no_e2e:
         x_host = x.cpu().pin_memory()
         out_host = torch.empty(T, c["d_in"], dtype=c["dtype"]).pin_memory()
         e_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
@@ -325,7 +404,7 @@ def run_ours(args, rank, world, device):
         def e2e_step(ev):
             ev[0].record(stream)
             xd = x_host.to(device, non_blocking=True)
-            out = forward(sae, xd)
+            out = sharded.forward(xd) if sharded is not None else forward(sae, xd)
             out_host.copy_(out, non_blocking=True)
             ev[1].record(stream)
 
@@ -342,10 +421,11 @@ def run_ours(args, rank, world, device):
             torch.distributed.all_reduce(e_tot, op=torch.distributed.ReduceOp.MAX)
         e_tot = float(e_tot.item())
         nbytes = T * c["d_in"] * x.element_size()
-        e2e = {"value": round(world * T * args.steps / (e_tot / 1e3), 1), "unit": "tokens/s",
+        api = ("FeatureShardedSAE.forward(x)" if sharded is not None else "saeflow_b200.forward(sae, x)")
+        e2e = {"value": round(job_tokens * args.steps / (e_tot / 1e3), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
                "ms_per_step": round(e_tot / args.steps, 4),
-               "api": "saeflow_b200.forward(sae, x) on pinned host x, result copied to pinned host"}
+               "api": f"{api} on pinned host x, result copied to pinned host (bytes per rank)"}
 
     err = device_error(device)
     if err:
@@ -359,7 +439,22 @@ def run_ours(args, rank, world, device):
     e = c["dtype"].itemsize if hasattr(c["dtype"], "itemsize") else torch.finfo(c["dtype"]).bits // 8
     stages = {}
     roofline = None
-    if cfg_id != 3:
+    if sharded is not None:
+        # Feature partition: every rank encodes all T tokens against its d_sae / world features;
+        # the step (encode + CSR + decode + all-reduce of partials) is timed as a whole.
+        n_feat = sharded.stop - sharded.start
+        flops = 2.0 * T * c["d_in"] * n_feat
+        step_mean = mean(step_ms)
+        achieved = flops / (step_mean / 1e3) / 1e12
+        tc_peak = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+        roofline = {"kernel": "whole feature-sharded step (encode GEMMs dominate)", "bound": "tensor",
+                    "achieved": round(achieved, 2), "peak": tc_peak, "unit": "TFLOP/s",
+                    "frac": round(achieved / tc_peak, 4), "traffic": None,
+                    "peak_source": f"{peak_src} bf16_tflops_sustained",
+                    "algorithmic": f"2*T*d_in*(d_sae/world) = {flops:.4g} FLOP per rank per step"}
+        stages["partition"] = f"feature: features [{sharded.start}, {sharded.stop}) on rank 0, " \
+                              f"all-reduce of fp32 partials per {args.chunk_tokens}-token chunk"
+    elif cfg_id != 3:
         flops = 2.0 * T * c["d_in"] * c["d_sae"]
         enc = mean(enc_ms)
         achieved = flops / (enc / 1e3) / 1e12
@@ -377,7 +472,9 @@ def run_ours(args, rank, world, device):
         stages["encode_ms"] = round(enc, 4)
         stages["encode_tflops"] = round(achieved, 2)
     dec = mean(dec_ms)
-    if cfg_id in (1, 2):
+    if sharded is not None:
+        nnz = None
+    elif cfg_id in (1, 2, 5):
         stages["csr_ms"] = round(mean(csr_ms), 4)
         nnz = step.nnz
         l0 = nnz / T
@@ -392,9 +489,10 @@ def run_ours(args, rank, world, device):
     else:
         l0 = c["k"]
         nnz = T * l0
-    dec_bytes = nnz * (c["d_in"] * e + 4 + e) + T * c["d_in"] * e + (T + 1) * 8
-    stages["decode_ms"] = round(dec, 4)
-    stages["decode_gbps_requested"] = round(dec_bytes / (dec / 1e3) / 1e9, 1)
+    if nnz is not None:
+        dec_bytes = nnz * (c["d_in"] * e + 4 + e) + T * c["d_in"] * e + (T + 1) * 8
+        stages["decode_ms"] = round(dec, 4)
+        stages["decode_gbps_requested"] = round(dec_bytes / (dec / 1e3) / 1e9, 1)
     if cfg_id == 3:
         hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
         roofline = {"kernel": "sparse decode (CSR gather)", "bound": "hbm",
@@ -403,15 +501,20 @@ def run_ours(args, rank, world, device):
                     "peak_source": f"{peak_src} hbm_gbs",
                     "algorithmic": "requested bytes L0*(d_in*e+4+e)+d_in*e+8 per token (bench_decode.py:57)"}
 
-    value = world * T * args.steps / (total_ms / 1e3)
+    value = job_tokens * args.steps / (total_ms / 1e3)
+    if sharded is not None:
+        parallelism = f"feature-sharded x{world}: d_sae/{world} features per rank, every rank encodes all " \
+                      "tokens, NCCL all-reduce of fp32 partial decodes"
+    else:
+        parallelism = f"token-sharded x{world}, weights replicated, no data-path collective"
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None,
+        "scaling": "strong" if cfg_id == 5 else "weak", "vs_baseline": None,
         "dtype": "bf16" if c["dtype"] == torch.bfloat16 else ("fp32" if c["dtype"] == torch.float32 else "fp16"),
         "data": "synthetic (seeded, BASELINE config distributions)",
-        "config": {"workload": c["name"], "tokens_per_gpu": T, "global_batch": world * T,
-                   "parallelism": f"token-sharded x{world}, weights replicated, no data-path collective",
+        "config": {"workload": c["name"], "tokens_per_gpu": T, "global_batch": job_tokens,
+                   "parallelism": parallelism,
                    "l2": "flushed between steps (256 MB write, outside the per-step events)"},
         "impl": "ours",
         "stages": stages,
@@ -421,7 +524,7 @@ def run_ours(args, rank, world, device):
         "clocks": clk.summary(),
         "wall_s_timed_region": round(wall, 3),
     }
-    if not args.no_cpu_baseline and world == 1:
+    if not args.no_cpu_baseline and world == 1 and cfg_id != 5:
         line["cpu_baseline"] = cpu_baseline(cfg_id, budget_s=args.cpu_seconds)
     return line
 
@@ -515,6 +618,10 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--partition", choices=["token", "feature"], default="token",
+                    help="config 5: token-sharded (weights replicated) or feature-sharded (d_sae split)")
+    ap.add_argument("--chunk-tokens", type=int, default=16384,
+                    help="config 5 feature partition: tokens per all-reduced chunk")
     ap.add_argument("--route", choices=["csr", "dense"], default="csr",
                     help="csr: encode straight to CSR (default); dense: dense features + compaction")
     args = ap.parse_args(argv)

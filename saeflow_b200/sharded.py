@@ -79,13 +79,19 @@ class FeatureShardedSAE:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        self.d_sae = sae.W_enc.shape[1]
-        self.start, self.stop = shard_range(self.d_sae, self.world, self.rank)
-        sl = slice(self.start, self.stop)
-        thr = sae.threshold[sl].contiguous() if sae.threshold is not None else None
-        self.local = _LocalSAE(W_enc=sae.W_enc[:, sl].contiguous(), b_enc=sae.b_enc[sl].contiguous(),
-                               W_dec=sae.W_dec[sl].contiguous(), b_dec=sae.b_dec, threshold=thr,
-                               activation=sae.activation)
+        start = getattr(sae, "feature_start", None)
+        if start is not None:
+            # Already this rank's slice (a caller that never holds the full weights).
+            self.start, self.stop = int(start), int(start) + sae.W_enc.shape[1]
+            self.local = _LocalSAE(W_enc=sae.W_enc, b_enc=sae.b_enc, W_dec=sae.W_dec, b_dec=sae.b_dec,
+                                   threshold=sae.threshold, activation=sae.activation)
+        else:
+            self.start, self.stop = shard_range(sae.W_enc.shape[1], self.world, self.rank)
+            sl = slice(self.start, self.stop)
+            thr = sae.threshold[sl].contiguous() if sae.threshold is not None else None
+            self.local = _LocalSAE(W_enc=sae.W_enc[:, sl].contiguous(), b_enc=sae.b_enc[sl].contiguous(),
+                                   W_dec=sae.W_dec[sl].contiguous(), b_dec=sae.b_dec, threshold=thr,
+                                   activation=sae.activation)
         self.ops = ops or _CudaOps()
         self.chunk_tokens = chunk_tokens
 
