@@ -272,9 +272,9 @@ def l2_flush(buf):
 # ------------------------------------------------------------------------------ our arm
 
 def run_ours(args, rank, world, device):
-    from saeflow_b200 import forward
+    from saeflow_b200 import forward_host
     from saeflow_b200.kernels import dense_to_csr, device_error, fused_encode, sparse_decode, topk_encode
-    from saeflow_b200.kernels.encode import encode_csr_finish, encode_csr_stage
+    from saeflow_b200.kernels.encode import encode_csr_finish_async, encode_csr_stage
 
     cfg_id = args.config
     c = CONFIGS[cfg_id]
@@ -354,16 +354,19 @@ def run_ours(args, rank, world, device):
         if cfg_id != 5:
             x = make_tokens(cfg_id, rank, device, T)
 
+        # What saeflow_b200.forward runs: the CSR stays on the device (no host sync mid-step).
         def step(ev):
             ev[0].record(stream)
-            h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation)
+            h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation,
+                                 device_consumer=True)
             ev[1].record(stream)
-            csr = encode_csr_finish(h)
+            indptr, indices, values, overflow = encode_csr_finish_async(h)
             ev[2].record(stream)
-            out = sparse_decode(*csr, sae.W_dec, sae.b_dec)
+            out = sparse_decode(indptr, indices, values, sae.W_dec, sae.b_dec)
             ev[3].record(stream)
-            step.nnz = csr[1].numel()
+            step.checks.append((indptr[-1], overflow))
             return out
+        step.checks = []
         launches_per_step = 5  # shift, encode+stage, indptr scan, place, decode
 
     def barrier():
@@ -384,6 +387,12 @@ def run_ours(args, rank, world, device):
             step(events[i])
         barrier()
         wall = time.perf_counter() - wall0
+    if getattr(step, "checks", None):
+        nnz_ovf = torch.stack([torch.stack([a, b.to(torch.int64)]) for a, b in step.checks]).cpu()
+        if int(nnz_ovf[:, 1].max()):
+            raise RuntimeError("CSR staging overflowed inside the timed region: the step did not do the work")
+        step.nnz = int(nnz_ovf[-1, 0])
+        step.checks.clear()
     step_ms = [e[0].elapsed_time(e[3]) for e in events]
     staged = cfg_id != 3 and sharded is None  # stage events recorded
     enc_ms = [e[0].elapsed_time(e[1]) for e in events] if staged else []
@@ -403,9 +412,10 @@ def run_ours(args, rank, world, device):
 
         def e2e_step(ev):
             ev[0].record(stream)
-            xd = x_host.to(device, non_blocking=True)
-            out = sharded.forward(xd) if sharded is not None else forward(sae, xd)
-            out_host.copy_(out, non_blocking=True)
+            if sharded is not None:
+                out_host.copy_(sharded.forward(x_host.to(device, non_blocking=True)), non_blocking=True)
+            else:
+                forward_host(sae, x_host, out_host, chunk_tokens=args.e2e_chunk)
             ev[1].record(stream)
 
         for _ in range(max(1, args.warmup)):
@@ -421,7 +431,8 @@ def run_ours(args, rank, world, device):
             torch.distributed.all_reduce(e_tot, op=torch.distributed.ReduceOp.MAX)
         e_tot = float(e_tot.item())
         nbytes = T * c["d_in"] * x.element_size()
-        api = ("FeatureShardedSAE.forward(x)" if sharded is not None else "saeflow_b200.forward(sae, x)")
+        api = ("FeatureShardedSAE.forward(x)" if sharded is not None else
+               f"saeflow_b200.forward_host(sae, x, out, chunk_tokens={args.e2e_chunk}) (copies overlapped with compute)")
         e2e = {"value": round(job_tokens * args.steps / (e_tot / 1e3), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
                "ms_per_step": round(e_tot / args.steps, 4),
@@ -618,6 +629,7 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunk", type=int, default=4096, help="forward_host chunk size (tokens)")
     ap.add_argument("--partition", choices=["token", "feature"], default="token",
                     help="config 5: token-sharded (weights replicated) or feature-sharded (d_sae split)")
     ap.add_argument("--chunk-tokens", type=int, default=16384,

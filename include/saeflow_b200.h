@@ -150,6 +150,22 @@ SF_API int sf_csr_place(const int32_t *tile_counts, const int32_t *tile_offsets,
                         int values_dtype, const int64_t *indptr, int32_t *indices, void *values, sf_stream stream);
 
 /*
+ * Encode straight to CSR, step 2 with no host sync, for a CSR consumed on the device (the
+ * forward pass decodes it right away): sf_csr_indptr on row_nnz followed by sf_csr_place,
+ * with indices / values sized by the staging capacity instead of by nnz (every placed pair
+ * comes from the staging, so nnz <= stage_capacity). If the staging overflowed (state[1] != 0,
+ * as written by sf_encode_csr_stage), indptr is written all zero and nothing is placed, so a
+ * decode that follows on the stream reads no entries; the caller reads state[1] after the
+ * stream work and redoes those rows through the dense route.
+ * Replaces the host sync of saeflow/kernels/decode.py:88 for device-side consumers
+ * (saeflow/ops.py:47-49 forward = decode_sparse(encode_sparse(x))).
+ */
+SF_API int sf_csr_finish_async(const int32_t *row_nnz, const int32_t *tile_counts, const int32_t *tile_offsets,
+                               int64_t M, int64_t d_sae, const int32_t *stage_indices, const void *stage_values,
+                               int64_t stage_capacity, int values_dtype, const uint32_t *state, int64_t *indptr,
+                               int32_t *indices, void *values, sf_stream stream);
+
+/*
  * row_nnz[m] = number of f[m, :] != 0 (NaN counts, -0.0 does not). Overwrites.
  * Replaces torch.count_nonzero at saeflow/kernels/decode.py:85.
  */

@@ -4,8 +4,8 @@ Drop-in for saeflow's `encode / encode_sparse / decode_sparse / forward` and
 `saeflow.kernels`, backed by hand-written CUDA kernels in libsaeflow_b200.so.
 """
 
-from .ops import decode_sparse, encode, encode_sparse, forward
+from .ops import decode_sparse, encode, encode_sparse, forward, forward_host
 from .sae import SAE
 
 __version__ = "0.1.0"
-__all__ = ["SAE", "decode_sparse", "encode", "encode_sparse", "forward"]
+__all__ = ["SAE", "decode_sparse", "encode", "encode_sparse", "forward", "forward_host"]

@@ -56,6 +56,8 @@ SIGNATURES = {
     "sf_encode_csr_stage": (_c.c_int, [_MP, _MP, _VP, _VP, _VP, _c.c_int, _c.c_int, _P, _P, _P, _P, _P,
                                        _c.c_int64, _P, _c.c_int, _P, _c.c_size_t, _P]),
     "sf_csr_place": (_c.c_int, [_P, _P, _c.c_int64, _c.c_int64, _P, _P, _c.c_int64, _c.c_int, _P, _P, _P, _P]),
+    "sf_csr_finish_async": (_c.c_int, [_P, _P, _P, _c.c_int64, _c.c_int64, _P, _P, _c.c_int64, _c.c_int, _P, _P,
+                                       _P, _P, _P]),
     "sf_row_nnz": (_c.c_int, [_MP, _P, _P]),
     "sf_csr_indptr": (_c.c_int, [_P, _c.c_int64, _P, _P]),
     "sf_dense_to_csr": (_c.c_int, [_MP, _P, _P, _P, _c.c_int, _P]),

@@ -13,7 +13,7 @@ namespace sf {
 
 // Defined in sparse.cu
 int launch_row_nnz(const sf_matrix &f, int32_t *row_nnz, cudaStream_t s);
-int launch_indptr(const int32_t *cnt, int64_t M, int64_t *indptr, cudaStream_t s);
+int launch_indptr(const int32_t *cnt, int64_t M, int64_t *indptr, cudaStream_t s, const unsigned *skip = nullptr);
 int launch_compact(const sf_matrix &f, const int64_t *indptr, int32_t *indices, void *values, int vdt,
                    cudaStream_t s);
 int launch_decode(const int64_t *indptr, int64_t M, const int32_t *indices, const void *values, int vdt,
@@ -23,7 +23,7 @@ int launch_topk_merge(const unsigned long long *cand, int64_t M, int ncand, int 
 int launch_topk_rows(const sf_matrix &f, int k, int32_t *out_idx, void *out_val, int vdt, cudaStream_t s);
 int launch_csr_place(const int32_t *tile_cnt, const int32_t *tile_off, int64_t n_tiles, const int32_t *stage_idx,
                      const void *stage_val, int64_t stage_cap, int vdt, const int64_t *indptr, int64_t M,
-                     int32_t *indices, void *values, cudaStream_t s);
+                     int32_t *indices, void *values, cudaStream_t s, const unsigned *skip = nullptr);
 
 namespace {
 thread_local char g_last_error[512] = "";
@@ -566,6 +566,26 @@ int sf_csr_place(const int32_t *tile_counts, const int32_t *tile_offsets, int64_
     const int64_t n_tiles = (d_sae + kCsrTile - 1) / kCsrTile;
     return launch_csr_place(tile_counts, tile_offsets, n_tiles, stage_indices, stage_values, stage_capacity,
                             values_dtype, indptr, M, indices, values, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int sf_csr_finish_async(const int32_t *row_nnz, const int32_t *tile_counts, const int32_t *tile_offsets, int64_t M,
+                        int64_t d_sae, const int32_t *stage_indices, const void *stage_values,
+                        int64_t stage_capacity, int values_dtype, const uint32_t *state, int64_t *indptr,
+                        int32_t *indices, void *values, sf_stream stream) {
+    if (M < 0 || d_sae < 0 || stage_capacity < 0) return set_error(SF_ERR_INVALID, "negative extent");
+    if (!valid_dtype(values_dtype)) return set_error(SF_ERR_INVALID, "bad values dtype %d", values_dtype);
+    if (!indptr || !state) return set_error(SF_ERR_INVALID, "NULL pointer");
+    if (M > 0 && (!row_nnz || !tile_counts || !tile_offsets))
+        return set_error(SF_ERR_INVALID, "NULL pointer");
+    if (stage_capacity > 0 && (!stage_indices || !stage_values || !indices || !values))
+        return set_error(SF_ERR_INVALID, "NULL staging or output pointer");
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const unsigned *overflow = reinterpret_cast<const unsigned *>(state) + 1;
+    int st = launch_indptr(row_nnz, M, indptr, s, overflow);
+    if (st || M == 0) return st;
+    const int64_t n_tiles = (d_sae + kCsrTile - 1) / kCsrTile;
+    return launch_csr_place(tile_counts, tile_offsets, n_tiles, stage_indices, stage_values, stage_capacity,
+                            values_dtype, indptr, M, indices, values, s, overflow);
 }
 
 int sf_row_nnz(const sf_matrix *f, int32_t *row_nnz, sf_stream stream) {

@@ -64,7 +64,7 @@ struct TcParams {
     int bm;               // rows per tile: 128 (single CTA) or 256 (CTA pair)
     int num_m_tiles, num_n_tiles;
     int num_kb;
-    int group_m;          // dense: raster group height in m-tiles
+    int group_m;          // raster group height in m-tiles
     int num_units;        // dense: tiles; topk: m_tiles * n_chunks
     int n_chunks, tiles_per_chunk;
     const void *b_enc;
@@ -124,9 +124,18 @@ __device__ __forceinline__ Unit unit_coords(const TcParams &p, int u, int mode) 
         r.n_count = 1;
         r.chunk = 0;
     } else {
-        // Chunks of one m-tile run side by side so concurrent units share x tiles in L2.
-        r.chunk = u % p.n_chunks;
-        r.m_blk = u / p.n_chunks;
+        // Grouped raster over (m-tile, column chunk) units, m fastest: the units running at
+        // once are group_m m-tiles on each of a few chunks, so each W_enc tile of a chunk is
+        // fetched from HBM once per group (its other group_m - 1 uses hit L2) and each x
+        // tile is shared by the chunks in flight. An m-tile-major order would instead pull
+        // all of W_enc from HBM once per m-tile.
+        const int per_group = p.group_m * p.n_chunks;
+        const int g = u / per_group;
+        const int first_m = g * p.group_m;
+        const int gm = min(p.num_m_tiles - first_m, p.group_m);
+        const int local = u - g * per_group;
+        r.m_blk = first_m + local % gm;
+        r.chunk = local / gm;
         r.n_first = r.chunk * p.tiles_per_chunk;
         r.n_count = min(p.tiles_per_chunk, p.num_n_tiles - r.n_first);
     }
@@ -1065,7 +1074,7 @@ int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, 
     if (st) return st;
     TcParams p{};
     fill_common(p, g, pair, device_error_word());
-    // x (A) stays L2-resident when a group of m-tiles fits in ~64 MB.
+    // x (A) stays L2-resident when a group of m-tiles fits in kRasterGroupBytes.
     const int es = g.ab_fmt == 2 ? 4 : 2;
     const int64_t a_tile_bytes = (int64_t)p.bm * g.K * es;
     p.group_m = (int)std::max<int64_t>(1, std::min<int64_t>(p.num_m_tiles, kRasterGroupBytes / std::max<int64_t>(1, a_tile_bytes)));
@@ -1153,7 +1162,12 @@ int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t strea
     if (st) return st;
     TcParams p{};
     fill_common(p, g, pair, device_error_word());
-    p.group_m = 1;
+    {
+        const int es = g.ab_fmt == 2 ? 4 : 2;
+        const int64_t a_tile_bytes = (int64_t)p.bm * g.K * es;
+        p.group_m = (int)std::max<int64_t>(
+            1, std::min<int64_t>(p.num_m_tiles, kRasterGroupBytes / std::max<int64_t>(1, a_tile_bytes)));
+    }
     const int chunks = tk.n_chunks;
     p.tiles_per_chunk = (p.num_n_tiles + chunks - 1) / chunks;
     p.n_chunks = (p.num_n_tiles + p.tiles_per_chunk - 1) / p.tiles_per_chunk;

@@ -173,6 +173,15 @@ __device__ __forceinline__ uint64_t l2_policy_evict_normal() {
     return p;
 }
 
+// 16-byte read-only global load with an L2 eviction-priority hint.
+__device__ __forceinline__ uint4 ld_nc_v4_hint(const void *ptr, uint64_t policy) {
+    uint4 r;
+    asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ptr), "l"(policy));
+    return r;
+}
+
 // 16-byte global store with an L2 eviction-priority hint.
 __device__ __forceinline__ void st_global_v4_hint(void *ptr, uint4 v, uint64_t policy) {
     asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y),

@@ -97,11 +97,18 @@ __global__ void row_nnz_kernel(const T *__restrict__ f, int64_t M, int64_t N, in
 
 // ------------------------------------------------------------------ indptr scan
 // Single CTA of 1024 threads; tiles of 4096 counts, carry in a register.
+// `skip` (may be NULL): when *skip is nonzero every row is written empty (indptr = 0), so a
+// decode that follows on the stream reads no entries (the CSR staging overflowed).
 __global__ void __launch_bounds__(1024) indptr_scan_kernel(const int32_t *__restrict__ cnt, int64_t M,
-                                                           int64_t *__restrict__ indptr, unsigned *err) {
+                                                           int64_t *__restrict__ indptr, unsigned *err,
+                                                           const unsigned *__restrict__ skip) {
     __shared__ long long warp_sums[32];
     __shared__ long long carry_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (skip != nullptr && *skip != 0u) {
+        for (int64_t i = tid; i <= M; i += blockDim.x) indptr[i] = 0;
+        return;
+    }
     if (tid == 0) {
         carry_s = 0;
         indptr[0] = 0;
@@ -239,6 +246,19 @@ __global__ void compact_kernel(const T *__restrict__ f, int64_t M, int64_t N, in
 // slice_start + (v*32 + l)*EPV, so each gathered W row is read as 32 x 16 B coalesced
 // segments; the row's (index, value) pairs are read 32 at a time and broadcast with
 // shuffles, and two W rows are kept in flight per step.
+// The slice width is chosen on the host so that one slice of every W_dec row fits in L2
+// (kDecodeL2Budget); the grid runs all rows of slice 0, then slice 1, ..., so each W_dec
+// row slice comes from HBM about once and its other uses hit L2.
+#ifndef SF_DECODE_WPOL
+#define SF_DECODE_WPOL 0  // W_dec loads: 0 default L2 policy, 1 evict_last
+#endif
+#ifndef SF_DECODE_OPOL
+#define SF_DECODE_OPOL 1  // output stores: 0 default L2 policy, 1 evict_first
+#endif
+__device__ __forceinline__ uint4 ld_w_v4(const void *p, uint64_t pol) {
+    if (SF_DECODE_WPOL) return ld_nc_v4_hint(p, pol);
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+}
 template <typename WT, typename VT, typename OT, int V>
 __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restrict__ indptr,
                                                          const int32_t *__restrict__ indices,
@@ -263,6 +283,7 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
     bool active[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) active[v] = d0 + (int64_t)(v * 32 + lane) * EPV < D;
+    const uint64_t wpol = SF_DECODE_WPOL ? l2_policy_evict_last() : 0ull;
 
     bool bad = false;
     for (int64_t j0 = start; j0 < end; j0 += 32) {
@@ -290,8 +311,8 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
             uint4 q0[V], q1[V];
 #pragma unroll
             for (int v = 0; v < V; ++v) {
-                q0[v] = active[v] ? __ldg(reinterpret_cast<const uint4 *>(r0 + v * 32 * EPV)) : make_uint4(0, 0, 0, 0);
-                q1[v] = active[v] ? __ldg(reinterpret_cast<const uint4 *>(r1 + v * 32 * EPV)) : make_uint4(0, 0, 0, 0);
+                q0[v] = active[v] ? ld_w_v4(r0 + v * 32 * EPV, wpol) : make_uint4(0, 0, 0, 0);
+                q1[v] = active[v] ? ld_w_v4(r1 + v * 32 * EPV, wpol) : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
             for (int v = 0; v < V; ++v) {
@@ -311,7 +332,7 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
 #pragma unroll
             for (int v = 0; v < V; ++v) {
                 if (!active[v]) continue;
-                const uint4 q = __ldg(reinterpret_cast<const uint4 *>(r0 + v * 32 * EPV));
+                const uint4 q = ld_w_v4(r0 + v * 32 * EPV, wpol);
                 const WT *e0 = reinterpret_cast<const WT *>(&q);
 #pragma unroll
                 for (int e = 0; e < EPV; ++e) acc[v][e] = fmaf(a0, to_f32(e0[e]), acc[v][e]);
@@ -335,7 +356,10 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
                 OT *o = reinterpret_cast<OT *>(&pk);
 #pragma unroll
                 for (int e = 0; e < EPV; ++e) o[e] = from_f32<OT>(r[e]);
-                *reinterpret_cast<uint4 *>(dst) = pk;
+                if (SF_DECODE_OPOL)
+                    st_global_v4_hint(dst, pk, l2_policy_evict_first());
+                else
+                    *reinterpret_cast<uint4 *>(dst) = pk;
             } else {
 #pragma unroll
                 for (int e = 0; e < EPV; ++e) dst[e] = from_f32<OT>(r[e]);
@@ -399,9 +423,10 @@ __global__ void csr_place_kernel(const int32_t *__restrict__ tile_cnt, const int
                                  int64_t n_tiles, const int32_t *__restrict__ stage_idx,
                                  const VT *__restrict__ stage_val, int64_t stage_cap,
                                  const int64_t *__restrict__ indptr, int64_t M, int32_t *__restrict__ indices,
-                                 VT *__restrict__ values, unsigned *err) {
+                                 VT *__restrict__ values, unsigned *err, const unsigned *__restrict__ skip) {
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= M) return;
+    if (skip != nullptr && *skip != 0u) return;  // staging overflowed: nothing to place
     const int lane = lane_id();
     const int64_t start = indptr[row], end = indptr[row + 1];
     int64_t run = start;
@@ -574,8 +599,8 @@ int launch_row_nnz(const sf_matrix &f, int32_t *row_nnz, cudaStream_t s) {
     });
 }
 
-int launch_indptr(const int32_t *cnt, int64_t M, int64_t *indptr, cudaStream_t s) {
-    indptr_scan_kernel<<<1, 1024, 0, s>>>(cnt, M, indptr, device_error_word());
+int launch_indptr(const int32_t *cnt, int64_t M, int64_t *indptr, cudaStream_t s, const unsigned *skip) {
+    indptr_scan_kernel<<<1, 1024, 0, s>>>(cnt, M, indptr, device_error_word(), skip);
     return check_cuda(cudaGetLastError(), "indptr scan launch");
 }
 
@@ -603,6 +628,10 @@ int launch_compact(const sf_matrix &f, const int64_t *indptr, int32_t *indices, 
         });
     });
 }
+
+// Bytes of W_dec one decode slice may span over all d_sae rows: half of the 126 MB L2, the
+// rest left to the CSR, the output stream and the other slice in flight at slice boundaries.
+constexpr int64_t kDecodeL2Budget = 64ll << 20;
 
 template <typename WT, typename VT, typename OT, int V>
 static int launch_decode_v(const int64_t *indptr, const int32_t *indices, const VT *values, const sf_matrix &W,
@@ -635,10 +664,18 @@ int launch_decode(const int64_t *indptr, int64_t M, const int32_t *indices, cons
                 if (vec) {
                     const int out_vec = ((out.stride_row * (int64_t)sizeof(OT)) % 16 == 0) &&
                                         (reinterpret_cast<uintptr_t>(out.data) & 15u) == 0;
-                    // Vectors per lane: split D into the fewest warp slices of <= 8 vectors/lane.
+                    // Vectors per lane: the widest slice (<= 8 vectors per lane) whose bytes
+                    // over all d_sae rows of W_dec fit the L2 budget (at least 1 vector),
+                    // then spread evenly over the slices that width needs.
                     const int64_t nvec = D / EPV;
-                    const int64_t slices = (nvec + 32 * 8 - 1) / (32 * 8);
+                    const int64_t row_slice_budget = kDecodeL2Budget / std::max<int64_t>(W.rows, 1);
+                    const int64_t vmax = std::min<int64_t>(8, std::max<int64_t>(1, row_slice_budget / (32 * 16)));
+                    const int64_t slices = (nvec + 32 * vmax - 1) / (32 * vmax);
+#ifdef SF_DECODE_V
+                    const int V = SF_DECODE_V;  // tuning builds only
+#else
                     const int V = (int)((nvec + 32 * slices - 1) / (32 * slices));
+#endif
                     switch (V) {
                         case 1: return launch_decode_v<WT, VT, OT, 1>(indptr, indices, vals, W, b, out, M, out_vec, s);
                         case 2: return launch_decode_v<WT, VT, OT, 2>(indptr, indices, vals, W, b, out, M, out_vec, s);
@@ -702,13 +739,13 @@ int launch_topk_rows(const sf_matrix &f, int k, int32_t *out_idx, void *out_val,
 namespace sf {
 int launch_csr_place(const int32_t *tile_cnt, const int32_t *tile_off, int64_t n_tiles, const int32_t *stage_idx,
                      const void *stage_val, int64_t stage_cap, int vdt, const int64_t *indptr, int64_t M,
-                     int32_t *indices, void *values, cudaStream_t s) {
+                     int32_t *indices, void *values, cudaStream_t s, const unsigned *skip) {
     if (M == 0) return SF_OK;
     return by_dtype(vdt, [&](auto tag) {
         using VT = decltype(tag);
         csr_place_kernel<VT><<<(unsigned)((M + 7) / 8), 256, 0, s>>>(
             tile_cnt, tile_off, n_tiles, stage_idx, reinterpret_cast<const VT *>(stage_val), stage_cap, indptr, M,
-            indices, reinterpret_cast<VT *>(values), device_error_word());
+            indices, reinterpret_cast<VT *>(values), device_error_word(), skip);
         return check_cuda(cudaGetLastError(), "csr place launch");
     });
 }

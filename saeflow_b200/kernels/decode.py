@@ -63,19 +63,24 @@ def _csr_operands(indptr, indices, values):
     return indptr, indices, values
 
 
-def sparse_decode(indptr, indices, values, W_dec, b_dec=None, *, out_dtype=None, config=None):
+def sparse_decode(indptr, indices, values, W_dec, b_dec=None, *, out_dtype=None, config=None, out=None):
     """CSR features @ W_dec (+ b_dec) -> [M, d_in], accumulated in fp32.
 
     W_dec: [d_sae, d_in], any strides (row-major is the fast case: gathered rows are
     contiguous 16-byte vectors). `config` is accepted for signature parity with the
     reference (decode.py:97) and has no effect: the kernel picks its D-slicing from d_in.
+    out: optional [M, d_in] CUDA tensor to write into (any strides; its dtype wins over
+    out_dtype). indices / values may be longer than indptr[M]: only indptr's ranges are read.
     """
     del config
     M = indptr.numel() - 1
     D = W_dec.shape[1]
     dev = _abi.require_cuda(("indptr", indptr), ("indices", indices), ("values", values), ("W_dec", W_dec),
-                            ("b_dec", b_dec))
-    out = torch.empty(M, D, device=dev, dtype=out_dtype or W_dec.dtype)
+                            ("b_dec", b_dec), ("out", out))
+    if out is None:
+        out = torch.empty(M, D, device=dev, dtype=out_dtype or W_dec.dtype)
+    elif tuple(out.shape) != (M, D):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, D)}")
     if M == 0:
         return out
     indptr, indices, values = _csr_operands(indptr, indices, values)

@@ -136,13 +136,15 @@ class _Staged:
     """Device buffers of an encode-straight-to-CSR call between its two steps."""
 
     __slots__ = ("args", "dev", "M", "N", "dtype", "row_nnz", "tile_cnt", "tile_off", "stage_idx", "stage_val",
-                 "state", "csr")
+                 "state", "csr", "stage_idx_out", "stage_val_out")
 
 
 def encode_csr_stage(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *, allow_tf32=None,
-                     stage_capacity=None):
+                     stage_capacity=None, device_consumer=False):
     """Step 1 of encode_csr: launches the shift pre-pass and the encoder GEMM with the CSR
-    staging epilogue (no host sync). Pass the result to encode_csr_finish."""
+    staging epilogue (no host sync). Pass the result to encode_csr_finish, or, with
+    device_consumer=True (which also allocates capacity-sized CSR outputs), to
+    encode_csr_finish_async."""
     if activation not in ACTIVATIONS:
         raise ValueError(f"fused_encode supports {list(ACTIVATIONS)}, got {activation!r}")
     if activation == "jumprelu" and threshold is None:
@@ -175,6 +177,9 @@ def encode_csr_stage(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", 
         h.stage_idx = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)
         h.stage_val = torch.empty(max(cap, 1), dtype=x.dtype, device=dev)
         h.state = torch.zeros(2, dtype=torch.int32, device=dev)
+        if device_consumer:
+            h.stage_idx_out = torch.empty_like(h.stage_idx)
+            h.stage_val_out = torch.empty_like(h.stage_val)
         need = ctypes.c_size_t(0)
         _abi.check(lib.sf_fused_encode_workspace(ctypes.byref(xm), ctypes.byref(wm), int(bool(allow_tf32)),
                                                  _abi.SF_VARIANT_AUTO, ctypes.byref(need)))
@@ -208,6 +213,26 @@ def encode_csr_finish(h):
                                         h.stage_val.data_ptr(), h.stage_idx.numel(), _abi.dtype_code(h.dtype, "values"),
                                         indptr.data_ptr(), indices.data_ptr(), values.data_ptr(), s))
     return indptr, indices, values
+
+
+def encode_csr_finish_async(h):
+    """Step 2 of encode_csr without the host sync, for a CSR consumed on the device:
+    (indptr, indices, values, overflow) where indices / values have the staging capacity as
+    length (only indptr's ranges are meaningful) and `overflow` is a device int32 scalar.
+    If it reads nonzero after the stream work, the staging overflowed, every row of the
+    returned CSR is empty, and the caller must redo the rows (encode_csr's dense route)."""
+    if h.csr is not None:
+        indptr, indices, values = h.csr
+        return indptr, indices, values, None
+    lib = _abi.load()
+    M, N, dev = h.M, h.N, h.dev
+    with torch.cuda.device(dev):
+        indptr = torch.empty(M + 1, dtype=torch.int64, device=dev)
+        _abi.check(lib.sf_csr_finish_async(
+            h.row_nnz.data_ptr(), h.tile_cnt.data_ptr(), h.tile_off.data_ptr(), M, N, h.stage_idx.data_ptr(),
+            h.stage_val.data_ptr(), h.stage_idx.numel(), _abi.dtype_code(h.dtype, "values"), h.state.data_ptr(),
+            indptr.data_ptr(), h.stage_idx_out.data_ptr(), h.stage_val_out.data_ptr(), _abi.stream_of(dev)))
+    return indptr, h.stage_idx_out, h.stage_val_out, h.state[1]
 
 
 def _dense_route(h):

@@ -5,9 +5,12 @@ activation, k), e.g. a saeflow.reference.SAE moved to a CUDA device.
 Sparse features are CSR tuples (indptr, indices, values); see kernels/decode.py.
 """
 
+import threading
+
 import torch
 
 from .kernels import encode_csr, fused_encode, sparse_decode, topk_encode
+from .kernels.encode import encode_csr_finish_async, encode_csr_stage
 
 
 def _topk(sae, x):
@@ -47,6 +50,108 @@ def decode_sparse(sae, csr):
     return sparse_decode(*csr, sae.W_dec, sae.b_dec)
 
 
+def _forward_async(sae, x, out=None, *, add_b_dec=True, out_dtype=None):
+    """forward() with every launch queued and no host sync: returns (x_hat, overflow), where
+    overflow is a device int32 scalar (None for routes that cannot overflow). A nonzero
+    overflow means the CSR staging ran out of room and x_hat holds only the bias.
+    add_b_dec=False gives the partial sum_j f_j W_dec[j] (feature-sharded decode)."""
+    b_dec = sae.b_dec if add_b_dec else None
+    if sae.activation == "topk":
+        csr, overflow = encode_sparse(sae, x), None
+    else:
+        h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation,
+                             device_consumer=True)
+        *csr, overflow = encode_csr_finish_async(h)
+    return sparse_decode(*csr, sae.W_dec, b_dec, out=out, out_dtype=out_dtype), overflow
+
+
 def forward(sae, x):
-    """encode_sparse then decode_sparse: the dense features never reach the decoder (ops.py:47-49)."""
-    return decode_sparse(sae, encode_sparse(sae, x))
+    """encode_sparse then decode_sparse: the dense features never reach the decoder (ops.py:47-49).
+
+    The CSR stays on the device between the two, so nothing waits on the host between the
+    encoder and the decoder; the one host read (as in the reference, decode.py:88) comes at
+    the end and checks that the CSR staging did not overflow (it then redoes the batch
+    through encode_sparse's exact-size route)."""
+    out, overflow = _forward_async(sae, x)
+    if overflow is not None and int(overflow):
+        out = decode_sparse(sae, encode_sparse(sae, x))
+    return out
+
+
+_copy_streams = {}
+_copy_lock = threading.Lock()
+
+
+def _streams(dev):
+    with _copy_lock:
+        if dev not in _copy_streams:
+            _copy_streams[dev] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        return _copy_streams[dev]
+
+
+def forward_host(sae, x, out=None, *, chunk_tokens=4096):
+    """forward() for a batch held in host memory, returning host memory.
+
+    x: [M, d_in] CPU tensor (pinned for the copies to overlap; pageable x is pinned first).
+    out: optional [M, d_in] pinned CPU tensor of W_dec's dtype to write into.
+    The batch runs in chunks of `chunk_tokens` rows on sae's device: chunk i+1's host-to-device
+    copy and chunk i-1's device-to-host copy run on their own streams while chunk i is encoded
+    and decoded on the current stream, with two device buffers per direction. One host sync at
+    the end waits for the last copy and reads every chunk's overflow flag; a chunk whose CSR
+    staging overflowed is redone through forward().
+    """
+    if x.is_cuda:
+        raise ValueError("forward_host takes a host tensor; call forward() for a device tensor")
+    if x.dim() != 2 or x.shape[1] != sae.W_enc.shape[0]:
+        raise ValueError(f"x must be [M, {sae.W_enc.shape[0]}], got {tuple(x.shape)}")
+    if chunk_tokens < 1:
+        raise ValueError("chunk_tokens must be positive")
+    dev = sae.W_enc.device
+    if dev.type != "cuda":
+        raise ValueError("the SAE's weights must be on a CUDA device")
+    M, D, dt = x.shape[0], sae.W_dec.shape[1], sae.W_dec.dtype
+    if out is None:
+        out = torch.empty(M, D, dtype=dt, pin_memory=True)
+    elif out.is_cuda or tuple(out.shape) != (M, D) or out.dtype != dt:
+        raise ValueError(f"out must be a host tensor [M, {D}] of {dt}")
+    if M == 0:
+        return out
+    if not x.is_pinned():
+        x = x.pin_memory()
+    compute = torch.cuda.current_stream(dev)
+    h2d, d2h = _streams(dev)
+    C = min(chunk_tokens, M)
+    xbuf = [torch.empty(C, x.shape[1], dtype=x.dtype, device=dev) for _ in range(2)]
+    obuf = [torch.empty(C, D, dtype=dt, device=dev) for _ in range(2)]
+    ev_in, ev_done, ev_out = [], [], []
+    flags = []
+    for i, r0 in enumerate(range(0, M, C)):
+        r1 = min(M, r0 + C)
+        n, s = r1 - r0, i % 2
+        ev_in.append(torch.cuda.Event())
+        ev_done.append(torch.cuda.Event())
+        ev_out.append(torch.cuda.Event())
+        with torch.cuda.stream(h2d):
+            if i >= 2:
+                h2d.wait_event(ev_done[i - 2])  # chunk i-2 has finished reading xbuf[s]
+            xbuf[s][:n].copy_(x[r0:r1], non_blocking=True)
+            ev_in[i].record(h2d)
+        compute.wait_event(ev_in[i])
+        if i >= 2:
+            compute.wait_event(ev_out[i - 2])  # chunk i-2's result has left obuf[s]
+        _, overflow = _forward_async(sae, xbuf[s][:n], obuf[s][:n])
+        ev_done[i].record(compute)
+        if overflow is not None:
+            flags.append((r0, r1, overflow))
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(ev_done[i])
+            out[r0:r1].copy_(obuf[s][:n], non_blocking=True)
+            ev_out[i].record(d2h)
+    compute.wait_stream(d2h)
+    compute.wait_stream(h2d)
+    bad = torch.stack([f for _, _, f in flags]).cpu().tolist() if flags else []  # the one host sync
+    torch.cuda.current_stream(dev).synchronize()
+    for (r0, r1, _), ovf in zip(flags, bad):
+        if ovf:
+            out[r0:r1].copy_(forward(sae, x[r0:r1].to(dev)))
+    return out

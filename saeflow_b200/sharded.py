@@ -64,6 +64,14 @@ class _CudaOps:
 
         return sparse_decode(*csr, W_dec, None, out_dtype=torch.float32)
 
+    @staticmethod
+    def partial_async(sae, x):
+        """fp32 partial decode of x against this rank's features (no b_dec) with the CSR kept
+        on the device: (partial, overflow flag as a device scalar or None), no host sync."""
+        from .ops import _forward_async
+
+        return _forward_async(sae, x, add_b_dec=False, out_dtype=torch.float32)
+
 
 class FeatureShardedSAE:
     """d_sae-sharded SAE over a process group (see module docstring).
@@ -100,16 +108,28 @@ class FeatureShardedSAE:
         indptr, indices, values = self.ops.encode_sparse(self.local, x)
         return indptr, indices + self.start, values
 
+    def _partial(self, x):
+        if hasattr(self.ops, "partial_async"):
+            return self.ops.partial_async(self.local, x)
+        return self.ops.decode_partial(self.ops.encode_sparse(self.local, x), self.local.W_dec), None
+
     def forward(self, x, out_dtype=None):
-        """x_hat for every token: partial decodes all-reduced over the ranks, + b_dec."""
+        """x_hat for every token: partial decodes all-reduced over the ranks, + b_dec.
+
+        The CSR of each chunk stays on the device (no host sync per chunk); one small
+        all-reduce(MAX) of the chunks' CSR-staging overflow flags at the end tells every rank
+        which chunks to redo through the exact-size route, so all ranks issue the same
+        collectives in the same order."""
         out_dtype = out_dtype or self.local.W_dec.dtype
         M = x.shape[0]
         out = torch.empty(M, self.local.W_dec.shape[1], dtype=out_dtype, device=x.device)
         pending = []  # (work, partial, row slice)
-        for r0 in range(0, M, self.chunk_tokens):
-            r1 = min(M, r0 + self.chunk_tokens)
-            csr = self.ops.encode_sparse(self.local, x[r0:r1])
-            partial = self.ops.decode_partial(csr, self.local.W_dec)
+        flags = []
+        chunks = [(r0, min(M, r0 + self.chunk_tokens)) for r0 in range(0, M, self.chunk_tokens)]
+        for r0, r1 in chunks:
+            partial, overflow = self._partial(x[r0:r1])
+            flags.append(overflow.reshape(1).to(torch.int32) if overflow is not None
+                         else torch.zeros(1, dtype=torch.int32, device=x.device))
             work = dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group, async_op=True) \
                 if self.world > 1 else None
             pending.append((work, partial, r0, r1))
@@ -118,6 +138,16 @@ class FeatureShardedSAE:
                 self._finish(pending.pop(0), out)
         while pending:
             self._finish(pending.pop(0), out)
+        if flags:
+            redo = torch.cat(flags)
+            if self.world > 1:
+                dist.all_reduce(redo, op=dist.ReduceOp.MAX, group=self.group)
+            for (r0, r1), bad in zip(chunks, redo.tolist()):
+                if bad:
+                    partial = self.ops.decode_partial(self.ops.encode_sparse(self.local, x[r0:r1]), self.local.W_dec)
+                    if self.world > 1:
+                        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+                    self._finish((None, partial, r0, r1), out)
         return out
 
     def _finish(self, item, out):

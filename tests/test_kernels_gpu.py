@@ -293,6 +293,82 @@ def test_encode_csr_strided_inputs_and_empty():
     assert ip.tolist() == [0] and ix.numel() == 0 and vs.numel() == 0
 
 
+def _sparse_sae(d_in, d_sae, activation, k=None):
+    """An SAE whose features fire on ~1% of tokens (well inside the default CSR staging)."""
+    sae = make_sae(d_in, d_sae, activation, torch.bfloat16, k=k).to("cuda")
+    if activation == "relu":
+        sae.b_enc.sub_(2.5)
+    elif activation == "jumprelu":
+        sae.threshold.add_(2.0)
+    return sae
+
+
+@pytest.mark.parametrize("activation", ["relu", "jumprelu"])
+@pytest.mark.parametrize("shape", [(37, 50, 129), (700, 256, 4099), (2000, 512, 8192)])
+def test_encode_csr_finish_async_matches_synced_csr(activation, shape):
+    """The sync-free finish (capacity-sized outputs) places the same pairs in the same slots
+    as the synced finish; indptr is identical and the overflow flag is clear."""
+    from saeflow_b200.kernels.encode import encode_csr_finish_async, encode_csr_stage
+
+    M, d_in, d_sae = shape
+    sae = _sparse_sae(d_in, d_sae, activation)
+    x = torch.randn(M, d_in, device="cuda").to(torch.bfloat16)
+    want = encode_csr(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, activation)
+    h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, activation, device_consumer=True)
+    ip, ix, vs, ovf = encode_csr_finish_async(h)
+    assert int(ovf) == 0
+    nnz = int(ip[-1])
+    assert ix.numel() >= nnz
+    _assert_same_csr((ip, ix[:nnz], vs[:nnz]), want)
+
+
+def test_forward_overflow_is_redone_and_flagged_csr_is_empty():
+    """Staging too small for the batch: the async finish writes an all-empty indptr (a decode
+    that follows reads nothing) and raises the flag; forward() redoes the batch correctly."""
+    from saeflow_b200 import forward
+    from saeflow_b200.kernels.encode import encode_csr_finish_async, encode_csr_stage
+
+    sae = make_sae(64, 600, "relu", torch.bfloat16).to("cuda")
+    sae.b_enc[:] = -5.0
+    sae.b_enc[:550] = 5.0  # > 512 active features per row: the default staging overflows
+    x = torch.randn(300, 64, device="cuda").to(torch.bfloat16)
+    h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, None, "relu", device_consumer=True)
+    ip, ix, vs, ovf = encode_csr_finish_async(h)
+    assert int(ovf) == 1
+    assert int(ip.abs().max()) == 0
+    rn = torch.zeros(300, device="cuda", dtype=torch.int32)
+    f = fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, row_nnz=rn)
+    want = sparse_decode(*dense_to_csr(f, rn), sae.W_dec, sae.b_dec)
+    got = forward(sae, x)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert device_error() == 0
+
+
+@pytest.mark.parametrize("activation", ["relu", "jumprelu", "topk"])
+@pytest.mark.parametrize("chunk", [64, 1000, 5000])
+def test_forward_host_matches_forward(activation, chunk):
+    """forward_host (pinned host in, host out, chunked with overlapped copies) gives bit for
+    bit the device forward() of the same chunks, for chunks smaller and larger than the
+    batch, and the whole-batch forward() within the bf16 tolerance."""
+    from saeflow_b200 import forward, forward_host
+
+    M, d_in, d_sae = 1500, 256, 4099
+    sae = _sparse_sae(d_in, d_sae, activation, k=16 if activation == "topk" else None)
+    x = torch.randn(M, d_in).to(torch.bfloat16)
+    want = torch.cat([forward(sae, x[r0:r0 + chunk].cuda()).cpu() for r0 in range(0, M, chunk)])
+    whole = forward(sae, x.cuda()).cpu()
+    got = forward_host(sae, x.pin_memory(), chunk_tokens=chunk)
+    torch.testing.assert_close(got.float(), whole.float(), atol=0.1, rtol=TOL[torch.bfloat16])
+    assert got.dtype == want.dtype and got.shape == want.shape and not got.is_cuda
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    out = torch.empty(M, d_in, dtype=torch.bfloat16).pin_memory()
+    forward_host(sae, x, out, chunk_tokens=chunk)  # pageable x is pinned internally
+    assert torch.equal(out.view(torch.int16), want.view(torch.int16))
+    with pytest.raises(ValueError):
+        forward_host(sae, x.cuda())
+    assert device_error() == 0
+
+
 # ----------------------------------------------------------------------------- decode
 
 @pytest.mark.parametrize("shape", SHAPES)

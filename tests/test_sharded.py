@@ -43,6 +43,42 @@ def _make(activation="jumprelu"):
     return sae, x
 
 
+class OverflowingOps(OracleOps):
+    """Device-style provider whose CSR staging 'overflows' on one chunk of rank 0 only: the
+    partial it returns for that chunk is garbage, and its flag says so. Every rank must then
+    redo that chunk (the flags are all-reduced) and the result must still be exact."""
+
+    def __init__(self, rank):
+        self.rank = rank
+        self.calls = 0
+
+    def partial_async(self, sae, x):
+        import oracle
+
+        bad = self.rank == 0 and self.calls == 1
+        self.calls += 1
+        partial = oracle.sparse_decode(*oracle.encode_sparse(sae, x), sae.W_dec, None, out_dtype=torch.float32)
+        if bad:
+            partial = torch.full_like(partial, 1e6)
+        return partial, torch.tensor(int(bad), dtype=torch.int32)
+
+
+def _worker_overflow(rank, init_file, q):
+    try:
+        import oracle
+        from saeflow_b200.sharded import FeatureShardedSAE
+
+        dist = _init(rank, init_file)
+        sae, x = _make("jumprelu")
+        fs = FeatureShardedSAE(sae, ops=OverflowingOps(rank), chunk_tokens=16)
+        got = fs.forward(x, out_dtype=torch.float32)
+        err = (got - oracle.forward(sae, x).float()).abs().max().item()
+        dist.destroy_process_group()
+        q.put((rank, "ok", err, True))
+    except Exception:  # noqa: BLE001
+        q.put((rank, "error", traceback.format_exc(), False))
+
+
 def _init(rank, init_file, timeout_s=20):
     import torch.distributed as dist
 
@@ -170,3 +206,11 @@ def test_dead_rank_surfaces_as_an_error_not_a_hang():
     assert rank0 is not None, "surviving rank never reported (hang)"
     assert rank0[1] == "raised", rank0
     assert time.time() - t0 < 90
+
+
+def test_feature_sharded_staging_overflow_on_one_rank_is_redone_by_all():
+    out = _run(_worker_overflow)
+    assert sorted(out) == [0, 1], out
+    for rank, status, err, _ in out.values():
+        assert status == "ok", err
+        assert err < 1e-5, f"rank {rank}: max error {err}"
