@@ -236,7 +236,8 @@ class ClockSampler:
                 sm = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
                 util = nv.nvmlDeviceGetUtilizationRates(self.handle).gpu
                 reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                self.samples.append((sm, util, reasons))
+                power_w = nv.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((sm, util, reasons, power_w))
             except Exception:  # noqa: BLE001
                 pass
             self.stop.wait(self.period)
@@ -261,7 +262,9 @@ class ClockSampler:
         for s in loaded:
             seen |= s[2]
         reasons = sorted(n for n, bit in self.REASONS.items() if seen & bit)
+        watts = sorted(s[3] for s in loaded)
         return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "power_w_median": round(watts[len(watts) // 2], 1),
                 "samples": len(self.samples), "samples_under_load": len(loaded), "source": "nvml 10 ms"}
 
 

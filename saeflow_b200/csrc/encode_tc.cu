@@ -47,6 +47,7 @@ constexpr int kThreads = 192;
 constexpr int kAccCols = 256;
 constexpr int kTmemCols = 512;
 constexpr int kTileABytes = kBM * 128;  // 128 rows x 128 B
+constexpr size_t kSmemOptin = 232448;   // opt-in shared memory per block on sm_100 (227 KB)
 constexpr int kTileBBytes = kBN * 128;  // 256 rows (or MN chunks) x 128 B
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
 
@@ -82,6 +83,7 @@ struct TcParams {
     unsigned *err;
     // topk
     int k;
+    int topk_buf;              // candidate buffer depth per row (entries)
     int values_dtype;
     unsigned long long *cand;  // [M, n_chunks, k] packed keys
     // csr (encode straight to CSR staging)
@@ -259,54 +261,113 @@ __device__ __forceinline__ void dense_chunk(const TcParams &p, const float *bias
     }
 }
 
-// Replaces this thread's smallest list entry (slot `slot`) by `key` and returns the new
-// smallest entry. Rare after the first tiles of a unit, so kept out of line.
-struct MinEntry {
-    unsigned long long key;
-    int slot;
+// Per-row top-k state of an epilogue thread. Its list of k packed (value, ~column) keys
+// lives in shared memory at topk_lists[s * 128 + et], unordered; `min_key` / `min_slot`
+// name its smallest entry once the list is full. Columns that beat the k-th largest seen so
+// far (`min_val`, refreshed at each merge) are appended to a per-row candidate buffer
+// (topk_buf[i * 128 + et]), and the buffers of a warp's 32 rows are merged into their lists
+// together, so one row's insertions never serialise the other 31 rows of the warp.
+struct TopkState {
+    unsigned long long min_key;  // smallest list key (0 while the list is not full)
+    int min_slot;
+    int fill;                    // list entries in use (< k while filling)
+    int cnt;                     // buffered candidates
+    float min_val;               // value part of min_key, -1 while the list is not full
 };
-__device__ __noinline__ MinEntry topk_insert(unsigned long long *topk_lists, int et, int k, int slot,
-                                             unsigned long long key) {
-    topk_lists[slot * 128 + et] = key;
-    MinEntry m{~0ull, 0};
-    for (int s = 0; s < k; ++s) {
-        const unsigned long long q = topk_lists[s * 128 + et];
-        if (q < m.key) {
-            m.key = q;
-            m.slot = s;
-        }
-    }
-    return m;
+
+__device__ __forceinline__ void topk_reset(TopkState &ts) {
+    ts.min_key = 0ull;
+    ts.min_slot = 0;
+    ts.fill = 0;
+    ts.cnt = 0;
+    ts.min_val = -1.f;
 }
 
 __device__ __forceinline__ float min_value_of(unsigned long long min_key) {
-    // An empty slot (key 0) lets every value in.
-    return min_key == 0ull ? -1.f : __uint_as_float(static_cast<uint32_t>(min_key >> 32));
+    return __uint_as_float(static_cast<uint32_t>(min_key >> 32));
 }
 
-// Top-k epilogue of one 32-column chunk: values are compared against the current k-th
-// largest in fp32 first (rounding is monotonic, so a value not above it cannot enter), and
-// only survivors build the packed (value, ~column) key.
-__device__ __forceinline__ void topk_chunk(const TcParams &p, const float *bias, const uint32_t (&r)[32], int col0,
-                                           unsigned long long *topk_lists, int et, unsigned long long &min_key,
-                                           int &min_slot) {
-    float min_val = min_value_of(min_key);
+// Smallest key of this thread's full list and its slot: four interleaved compare chains
+// over independent shared-memory loads.
+__device__ __forceinline__ void topk_rescan(const unsigned long long *lists, int et, int k, TopkState &ts) {
+    unsigned long long m[4] = {~0ull, ~0ull, ~0ull, ~0ull};
+    int ms[4] = {0, 0, 0, 0};
+    int s = 0;
+#pragma unroll 2
+    for (; s + 4 <= k; s += 4) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const int col = col0 + j;
-        const float o = fmaxf(__uint_as_float(r[j]) + bias[j], 0.f);
-        if (o > min_val && col < p.N) {
-            const float v = round_to(o, p.values_dtype);
-            const unsigned long long key =
-                (static_cast<unsigned long long>(__float_as_uint(v) & 0x7FFFFFFFu) << 32) |
-                static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
-            if (key > min_key) {
-                const MinEntry m = topk_insert(topk_lists, et, p.k, min_slot, key);
-                min_key = m.key;
-                min_slot = m.slot;
-                min_val = min_value_of(min_key);
+        for (int c = 0; c < 4; ++c) {
+            const unsigned long long q = lists[(s + c) * 128 + et];
+            if (q < m[c]) {
+                m[c] = q;
+                ms[c] = s + c;
             }
         }
+    }
+    for (; s < k; ++s) {
+        const unsigned long long q = lists[s * 128 + et];
+        if (q < m[0]) {
+            m[0] = q;
+            ms[0] = s;
+        }
+    }
+#pragma unroll
+    for (int c = 1; c < 4; ++c) {
+        if (m[c] < m[0]) {
+            m[0] = m[c];
+            ms[0] = ms[c];
+        }
+    }
+    ts.min_key = m[0];
+    ts.min_slot = ms[0];
+}
+
+// Merges this thread's buffered candidates (in column order) into its list: the first k
+// fill the list, each later one replaces the smallest entry when it is larger. Out of line
+// and by value, so the state stays in registers on the per-column path.
+__device__ __noinline__ TopkState topk_merge_buffer(unsigned long long *lists, const unsigned long long *buf,
+                                                    int et, int k, TopkState ts) {
+    for (int i = 0; i < ts.cnt; ++i) {
+        const unsigned long long key = buf[i * 128 + et];
+        if (ts.fill < k) {
+            lists[ts.fill * 128 + et] = key;
+            if (++ts.fill == k) topk_rescan(lists, et, k, ts);
+        } else if (key > ts.min_key) {
+            lists[ts.min_slot * 128 + et] = key;
+            topk_rescan(lists, et, k, ts);
+        }
+    }
+    ts.cnt = 0;
+    ts.min_val = ts.fill < k ? -1.f : min_value_of(ts.min_key);
+    return ts;
+}
+
+// Top-k epilogue of one 32-column chunk, in groups of kTopkGroup columns: values are
+// compared against the k-th largest of the previous merge in fp32 (rounding is monotonic,
+// so a value not above it cannot enter) and survivors are buffered as packed keys. After
+// each group the warp merges its buffers if any row's buffer could overflow on the next
+// group (the host guarantees topk_buf >= kTopkGroup).
+constexpr int kTopkGroup = 8;
+__device__ __forceinline__ void topk_chunk(const TcParams &p, const float *bias, const uint32_t (&r)[32], int col0,
+                                           unsigned long long *topk_lists, int et, TopkState &ts) {
+    unsigned long long *buf = topk_lists + p.k * 128;
+#pragma unroll
+    for (int g = 0; g < 32; g += kTopkGroup) {
+        const float min_val = ts.min_val;
+#pragma unroll
+        for (int j = g; j < g + kTopkGroup; ++j) {
+            const int col = col0 + j;
+            const float o = fmaxf(__uint_as_float(r[j]) + bias[j], 0.f);
+            if (o > min_val && col < p.N) {
+                const float v = round_to(o, p.values_dtype);
+                buf[ts.cnt * 128 + et] =
+                    (static_cast<unsigned long long>(__float_as_uint(v) & 0x7FFFFFFFu) << 32) |
+                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col));
+                ++ts.cnt;
+            }
+        }
+        if (__any_sync(0xffffffffu, ts.cnt > p.topk_buf - kTopkGroup))
+            ts = topk_merge_buffer(topk_lists, buf, et, p.k, ts);
     }
 }
 
@@ -412,7 +473,7 @@ __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, 
 template <int MODE, typename OT, bool JUMP, typename Release>
 __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
                                                 int et, int row, int n_blk, int buf, uint32_t taddr,
-                                                uint64_t pol_out, unsigned long long &min_key, int &min_slot,
+                                                uint64_t pol_out, TopkState &ts,
                                                 Release release) {
     constexpr int NC = kBN / 32;
     const bool full_tile = (n_blk + 1) * kBN <= p.N;
@@ -426,7 +487,7 @@ __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShare
             else
                 dense_chunk<OT, JUMP, false>(p, bias, &sh->thr[buf][c * 32], r, row, col0, pol_out, cnt);
         } else {
-            topk_chunk(p, bias, r, col0, topk_lists, et, min_key, min_slot);
+            topk_chunk(p, bias, r, col0, topk_lists, et, ts);
         }
     };
     // Two register buffers: the load of the next chunk is in flight while one is processed.
@@ -451,7 +512,7 @@ __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShare
 template <int MODE, typename Release>
 __device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
                                               int et, int row, int n_blk, int buf, uint32_t taddr, uint64_t pol_out,
-                                              unsigned long long &min_key, int &min_slot, Release release) {
+                                              TopkState &ts, Release release) {
     if constexpr (MODE == kCsr) {
         if (p.out_dtype == SF_BF16)
             csr_tile<__nv_bfloat16>(p, sh, row, n_blk, buf, taddr, release);
@@ -462,32 +523,27 @@ __device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared 
         return;
     }
     if constexpr (MODE == kTopk) {
-        epilogue_tile_t<kTopk, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
-                                             min_slot, release);
+        epilogue_tile_t<kTopk, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
         return;
     }
     const bool jump = p.activation == SF_ACT_JUMPRELU;
     if (p.out_dtype == SF_BF16) {
         if (jump)
             epilogue_tile_t<kDense, __nv_bfloat16, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
-                                                         min_key, min_slot, release);
+                                                         ts, release);
         else
             epilogue_tile_t<kDense, __nv_bfloat16, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
-                                                          min_key, min_slot, release);
+                                                          ts, release);
     } else if (p.out_dtype == SF_F16) {
         if (jump)
-            epilogue_tile_t<kDense, __half, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
-                                                  min_slot, release);
+            epilogue_tile_t<kDense, __half, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
         else
-            epilogue_tile_t<kDense, __half, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
-                                                   min_slot, release);
+            epilogue_tile_t<kDense, __half, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
     } else {
         if (jump)
-            epilogue_tile_t<kDense, float, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
-                                                 min_slot, release);
+            epilogue_tile_t<kDense, float, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
         else
-            epilogue_tile_t<kDense, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key,
-                                                  min_slot, release);
+            epilogue_tile_t<kDense, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
     }
 }
 
@@ -651,8 +707,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
             const Unit un = unit_coords(p, u, MODE);
             const int row = un.m_blk * kBM + row_in_tile;
-            unsigned long long min_key = 0;
-            int min_slot = 0;
+            TopkState ts;
+            topk_reset(ts);
             if (MODE == kTopk) {
                 for (int s = 0; s < p.k; ++s) topk_lists[s * 128 + et] = 0ull;
             }
@@ -668,7 +724,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
                 const int acc_now = acc;
-                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key, min_slot, [&] {
+                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, [&] {
                     tc_fence_before();
                     mbar_arrive(&sh->tmem_empty[acc_now]);
                 });
@@ -677,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc_phase ^= 1u;
                 }
             }
+            if (MODE == kTopk && ok) ts = topk_merge_buffer(topk_lists, topk_lists + p.k * 128, et, p.k, ts);
             if (MODE == kTopk && ok && row < p.M) {
                 unsigned long long *dst = p.cand + ((int64_t)row * p.n_chunks + un.chunk) * p.k;
                 for (int s = 0; s < p.k; ++s) dst[s] = topk_lists[s * 128 + et];
@@ -882,8 +939,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = pair; ok && u < p.num_units; u += npairs) {
             const Unit un = unit_coords(p, u, MODE);
             const int row = un.m_blk * 256 + row_in_tile;
-            unsigned long long min_key = 0;
-            int min_slot = 0;
+            TopkState ts;
+            topk_reset(ts);
             if (MODE == kTopk) {
                 for (int s = 0; s < p.k; ++s) topk_lists[s * 128 + et] = 0ull;
             }
@@ -899,7 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
                 const uint32_t empty_leader = map_to_rank(smem_u32(&sh->tmem_empty[acc]), 0);
-                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, min_key, min_slot, [&] {
+                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, [&] {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_remote(empty_leader);
@@ -909,6 +966,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc_phase ^= 1u;
                 }
             }
+            if (MODE == kTopk && ok) ts = topk_merge_buffer(topk_lists, topk_lists + p.k * 128, et, p.k, ts);
             if (MODE == kTopk && ok && row < p.M) {
                 unsigned long long *dst = p.cand + ((int64_t)row * p.n_chunks + un.chunk) * p.k;
                 for (int s = 0; s < p.k; ++s) dst[s] = topk_lists[s * 128 + et];
@@ -1130,8 +1188,12 @@ int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &
     return dispatch<kCsr, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
 }
 
-// Column chunks per row for the top-k schedule: enough (m-tile, chunk) units to fill the
-// available CTAs (or CTA pairs) in whole waves.
+// Column chunks per row for the top-k schedule. Each (m-tile, chunk) unit starts its rows'
+// top-k lists empty, and filling them is the epilogue's expensive phase (most columns enter
+// while the list is young), so use the FEWEST chunks whose units still fill the available
+// CTAs (or CTA pairs) in whole waves to within kTopkWaveEff; failing that, the best-balanced
+// count up to 32.
+constexpr double kTopkWaveEff = 0.94;
 int topk_chunks(int64_t M, int64_t N) {
     const bool pair = M > kBM;
     const int bm = pair ? 256 : kBM;
@@ -1145,8 +1207,8 @@ int topk_chunks(int64_t M, int64_t N) {
         const int chunks = (n_tiles + tpc - 1) / tpc;
         const long units = (long)m_tiles * chunks;
         const long waves = (units + slots - 1) / slots;
-        double eff = (double)units / (double)(waves * slots);
-        eff -= 0.002 * c;  // prefer fewer candidates at equal balance
+        const double eff = (double)units / (double)(waves * slots);
+        if (eff >= kTopkWaveEff) return chunks;
         if (eff > best_eff + 1e-9) {
             best_eff = eff;
             best = chunks;
@@ -1181,14 +1243,29 @@ int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t strea
     p.values_dtype = tk.values_dtype;
     p.cand = tk.cand;
     if (tk.k < 1 || tk.k > kTopkMaxK) return set_error(SF_ERR_UNSUPPORTED, "fused top-k supports 1 <= k <= %d", kTopkMaxK);
-    const size_t lists = (size_t)tk.k * 128 * sizeof(unsigned long long);
+    // Shared memory per CTA: the operand ring, TcShared, the k-entry lists and a candidate
+    // buffer of topk_buf entries per row (1 KB per entry over the 128 rows). The ring keeps
+    // the most stages that still leave a buffer of >= 48 entries (up to 64).
+    const size_t stage_bytes = pair ? (size_t)(kBM * 128 + (kBN / 2) * 128) : (size_t)kStageBytes;
+    const size_t row_entry = 128 * sizeof(unsigned long long);
+    auto buffer_for = [&](int stages) -> long {
+        const long left = (long)kSmemOptin - 1024 - (long)(stages * stage_bytes) - (long)sizeof(TcShared) -
+                          (long)(tk.k * row_entry);
+        return std::min<long>(64, left / (long)row_entry);
+    };
+    int stages = pair ? 4 : 3;
+    while (stages > 2 && buffer_for(stages) < 48) --stages;
+    if (buffer_for(stages) < kTopkGroup)
+        return set_error(SF_ERR_UNSUPPORTED, "top-k k=%d does not fit in shared memory", tk.k);
+    p.topk_buf = (int)buffer_for(stages);
+    const size_t extra = (size_t)(tk.k + p.topk_buf) * row_entry;
     if (pair) {
-        if (tk.k <= 32) return dispatch<kTopk, 4, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
-        if (tk.k <= 64) return dispatch<kTopk, 4, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
-        return dispatch<kTopk, 3, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+        if (stages == 4) return dispatch<kTopk, 4, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
+        if (stages == 3) return dispatch<kTopk, 3, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
+        return dispatch<kTopk, 2, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
     }
-    if (tk.k <= 64) return dispatch<kTopk, 3, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
-    return dispatch<kTopk, 2, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, lists, stream);
+    if (stages == 3) return dispatch<kTopk, 3, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
+    return dispatch<kTopk, 2, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
 }
 
 }  // namespace sf

@@ -62,7 +62,7 @@ int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &
 int pair_slots(const void *kern, const cudaLaunchConfig_t &cfg);
 int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t stream);
 int topk_chunks(int64_t M, int64_t N);
-constexpr int kTopkMaxK = 120;  // shared-memory bound of the fused top-k lists
+constexpr int kTopkMaxK = 112;  // shared-memory bound of the fused top-k lists and candidate buffers
 
 int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
                     int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream);
