@@ -1,0 +1,337 @@
+"""Activation caching with on-the-fly SAE encoding: a drop-in for saeflow/cache.py.
+
+The directory layout, manifest, shard atomicity, resume rule and reader are the
+reference's (saeflow/cache.py:1-14, :39-45, :70-137, :140-194), because other tools read
+this format:
+
+    manifest.json                                   config + list of finished shards
+    <hook>/<shard:05d>.npy                          dense activations [rows, d]
+    <hook>/<shard:05d>.{indptr,indices,values}.npy  CSR SAE features [rows, d_sae]
+
+A row is one token position, in sequence-major order; a shard covers
+`batches_per_shard` forward batches; bf16 is stored as its raw int16 bits (numpy has no
+bf16; the manifest records the dtype). Shard files are fsynced and renamed into place
+before the manifest records the shard, so after an interruption the cache holds only
+whole shards and a rerun with the same arguments resumes at the first missing one.
+
+What differs is how the GPU is kept busy. The reference copies every batch's result to
+the host synchronously and writes each shard before computing the next
+(cache.py:118-137). Here:
+
+* encoded hooks run `saeflow_b200.encode_sparse` (the encoder GEMM writing CSR straight
+  from its epilogue) on the SAE's device;
+* each device-to-host copy (dense activations, the three CSR arrays) is queued on a copy
+  stream into pinned host memory, so the next batch's model forward and encode overlap it;
+* one writer thread waits for a shard's copies, assembles it, writes and fsyncs its files
+  and then the manifest, in shard order, while the next shard is computed. If the
+  producer fails, the shards already handed to the writer are still completed before the
+  error propagates, so the cache again holds only whole shards.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import queue
+import re
+import threading
+from pathlib import Path
+
+import numpy as np
+import torch
+
+_DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+_CSR_PARTS = ("indptr", "indices", "values")
+_WRITE_AHEAD = 2  # shards that may wait for the writer before the producer blocks
+
+
+def _encode_sparse(sae, x):
+    """The on-the-fly encoder (tests substitute a CPU restatement)."""
+    from .ops import encode_sparse
+
+    return encode_sparse(sae, x)
+
+
+# ----------------------------------------------------------------------------- host side
+
+def _to_numpy(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().contiguous().cpu()
+    return (t.view(torch.int16) if t.dtype == torch.bfloat16 else t).numpy()
+
+
+def _from_numpy(a, dtype) -> torch.Tensor:
+    t = torch.from_numpy(np.array(a))  # a copy: the shard arrays are read-only memory maps
+    return t.view(dtype) if dtype == torch.bfloat16 else t
+
+
+def _atomic_write(path: Path, write) -> None:
+    tmp = path.with_name(path.name + ".tmp")
+    with open(tmp, "wb") as fh:
+        write(fh)
+        fh.flush()
+        os.fsync(fh.fileno())
+    os.replace(tmp, path)
+
+
+def _save(path: Path, t: torch.Tensor) -> None:
+    _atomic_write(path, lambda fh: np.save(fh, _to_numpy(t)))
+
+
+def _cat_csr(parts):
+    """Row-wise concatenation of CSR blocks (indptr rebased onto one running offset)."""
+    indptrs, offset = [torch.zeros(1, dtype=torch.int64)], 0
+    for indptr, _, _ in parts:
+        indptrs.append(indptr[1:].cpu().to(torch.int64) + offset)
+        offset += int(indptr[-1])
+    return (torch.cat(indptrs), torch.cat([p[1].cpu() for p in parts]), torch.cat([p[2].cpu() for p in parts]))
+
+
+def _stop_layer(hook_names):
+    """Blocks the forward needs for the deepest requested hook (None: run them all)."""
+    layers = [re.match(r"blocks\.(\d+)\.", h) for h in hook_names]
+    return max(int(m.group(1)) for m in layers) + 1 if all(layers) else None
+
+
+# ----------------------------------------------------------------------------- async copies
+
+class _HostCopy:
+    """A device tensor on its way to pinned host memory (or a host tensor as is)."""
+
+    __slots__ = ("host", "event", "_src")
+
+    def __init__(self, t: torch.Tensor, streams: dict):
+        if not t.is_cuda:
+            self.host, self.event, self._src = t.detach().contiguous(), None, None
+            return
+        dev = t.device
+        stream = streams.get(dev)
+        if stream is None:
+            stream = streams[dev] = torch.cuda.Stream(dev)
+        src = t.detach().contiguous()
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        self.host = torch.empty(src.shape, dtype=src.dtype, pin_memory=True)
+        with torch.cuda.stream(stream):
+            self.host.copy_(src, non_blocking=True)
+            self.event = torch.cuda.Event()
+            self.event.record(stream)
+        src.record_stream(stream)  # the allocator must not reuse src before the copy ends
+        self._src = src
+
+    def wait(self) -> torch.Tensor:
+        if self.event is not None:
+            self.event.synchronize()
+            self.event, self._src = None, None
+        return self.host
+
+
+class _ShardWriter:
+    """One thread that assembles, writes and records shards in submission order."""
+
+    def __init__(self, out_dir: Path, manifest: dict):
+        self.out_dir, self.manifest = out_dir, manifest
+        self.jobs: queue.Queue = queue.Queue(maxsize=_WRITE_AHEAD)
+        self.error: BaseException | None = None
+        self.thread = threading.Thread(target=self._run, name="saeflow-cache-writer", daemon=True)
+        self.thread.start()
+
+    def submit(self, job) -> None:
+        if self.error is not None:
+            raise RuntimeError("the cache writer failed") from self.error
+        self.jobs.put(job)
+
+    def close(self) -> None:
+        self.jobs.put(None)
+        self.thread.join()
+        if self.error is not None:
+            raise RuntimeError("the cache writer failed") from self.error
+
+    def _run(self) -> None:
+        while True:
+            job = self.jobs.get()
+            if job is None:
+                return
+            if self.error is not None:
+                continue  # drain: nothing after a failed shard may be recorded
+            try:
+                self._write(*job)
+            except BaseException as e:  # noqa: BLE001 - reported to the producer
+                self.error = e
+
+    def _write(self, shard: int, parts: dict, hooks_meta: dict, n_seqs: int, n_rows: int) -> None:
+        for h, pieces in parts.items():
+            if hooks_meta[h]["format"] == "csr":
+                csr = _cat_csr([tuple(c.wait() for c in piece) for piece in pieces])
+                for name, t in zip(_CSR_PARTS, csr):
+                    _save(self.out_dir / h / f"{shard:05d}.{name}.npy", t)
+            else:
+                _save(self.out_dir / h / f"{shard:05d}.npy", torch.cat([c.wait() for c in pieces]))
+            self.manifest["hooks"][h] = hooks_meta[h]
+        self.manifest["shards"].append({"n_seqs": n_seqs, "n_rows": n_rows})
+        text = json.dumps(self.manifest, indent=2).encode()
+        _atomic_write(self.out_dir / "manifest.json", lambda fh: fh.write(text))
+
+
+# ----------------------------------------------------------------------------- writer API
+
+@torch.inference_mode()
+def cache_activations(model, tokens, hook_names, out_dir, *, batch_size=8, batches_per_shard=32,
+                      dtype=torch.float32, encoders=None):
+    """Run `model` over `tokens` [n_seqs, seq_len] and cache activations at `hook_names`.
+
+    model: a TransformerLens HookedTransformer, or anything with a compatible
+      `run_with_cache(batch, names_filter=, stop_at_layer=, return_type=None)` and
+      `parameters()`.
+    encoders: optional {hook_name: sae}; those hooks are SAE-encoded on the fly on the
+      SAE's device and stored as CSR feature activations instead of dense ones.
+    Calling again with the same arguments after an interruption resumes the run.
+    Returns the cache directory as a Path. Same arguments, errors and files as
+    saeflow.cache.cache_activations (cache.py:70-137).
+    """
+    out_dir, hook_names, encoders = Path(out_dir), list(hook_names), encoders or {}
+    unknown = set(encoders) - set(hook_names)
+    if unknown:
+        raise ValueError(f"encoders given for hooks not being cached: {sorted(unknown)}")
+    config = {
+        "hook_names": hook_names,
+        "n_seqs": len(tokens),
+        "seq_len": int(tokens.shape[1]),
+        "batch_size": batch_size,
+        "batches_per_shard": batches_per_shard,
+        "dtype": str(dtype).removeprefix("torch."),
+        "encoded": sorted(encoders),
+    }
+    manifest_path = out_dir / "manifest.json"
+    if manifest_path.exists():
+        manifest = json.loads(manifest_path.read_text())
+        if manifest["config"] != config:
+            raise ValueError(f"{out_dir} holds a cache with a different config: {manifest['config']}")
+    else:
+        manifest = {"config": config, "hooks": {}, "shards": []}
+    for h in hook_names:
+        (out_dir / h).mkdir(parents=True, exist_ok=True)
+
+    device = next(model.parameters()).device
+    stop = _stop_layer(hook_names)
+    seqs_per_shard = batch_size * batches_per_shard
+    first_shard = len(manifest["shards"])
+    streams: dict = {}
+    writer = _ShardWriter(out_dir, manifest)
+    try:
+        shard = first_shard
+        for start in range(first_shard * seqs_per_shard, len(tokens), seqs_per_shard):
+            end = min(start + seqs_per_shard, len(tokens))
+            parts = {h: [] for h in hook_names}
+            meta = {}
+            for b in range(start, end, batch_size):
+                batch = tokens[b:min(b + batch_size, end)].to(device)
+                _, acts = model.run_with_cache(batch, names_filter=hook_names, stop_at_layer=stop, return_type=None)
+                for h in hook_names:
+                    a = acts[h].flatten(0, 1).flatten(1)  # [batch * pos, d]; per-head hooks are concatenated
+                    if h in encoders:
+                        sae = encoders[h]
+                        indptr, indices, values = _encode_sparse(sae, a.to(sae.W_enc.device, sae.W_enc.dtype))
+                        parts[h].append((_HostCopy(indptr, streams), _HostCopy(indices, streams),
+                                         _HostCopy(values.to(dtype), streams)))
+                        meta[h] = {"format": "csr", "d": int(sae.W_enc.shape[1])}
+                    else:
+                        parts[h].append(_HostCopy(a.to(dtype), streams))
+                        meta[h] = {"format": "dense", "d": int(a.shape[1])}
+            writer.submit((shard, parts, meta, end - start, (end - start) * config["seq_len"]))
+            shard += 1
+    finally:
+        writer.close()
+    return out_dir
+
+
+# ----------------------------------------------------------------------------- reader
+
+class ActivationReader:
+    """Streams a cache written by cache_activations (here or by saeflow) back as batches."""
+
+    def __init__(self, path):
+        self.path = Path(path)
+        self.manifest = json.loads((self.path / "manifest.json").read_text())
+        self.dtype = _DTYPES[self.manifest["config"]["dtype"]]
+
+    @property
+    def hook_names(self):
+        return self.manifest["config"]["hook_names"]
+
+    def n_rows(self):
+        return sum(s["n_rows"] for s in self.manifest["shards"])
+
+    def _is_csr(self, hook):
+        return self.manifest["hooks"][hook]["format"] == "csr"
+
+    def _open(self, hook, shard):
+        d = self.path / hook
+        if self._is_csr(hook):
+            return [np.load(d / f"{shard:05d}.{name}.npy", mmap_mode="r") for name in _CSR_PARTS]
+        return np.load(d / f"{shard:05d}.npy", mmap_mode="r")
+
+    def _rows(self, hook, arrays, a, b):
+        if not self._is_csr(hook):
+            return _from_numpy(arrays[a:b], self.dtype)
+        indptr, indices, values = arrays
+        lo, hi = int(indptr[a]), int(indptr[b])
+        return (torch.from_numpy(np.array(indptr[a:b + 1]) - lo), torch.from_numpy(np.array(indices[lo:hi])),
+                _from_numpy(values[lo:hi], self.dtype))
+
+    def _join(self, hook, pieces):
+        return _cat_csr(pieces) if self._is_csr(hook) else torch.cat(pieces)
+
+    def _host_batches(self, hook, batch_size):
+        pending, n_pending = [], 0
+        for i, shard in enumerate(self.manifest["shards"]):
+            arrays, row = self._open(hook, i), 0
+            while row < shard["n_rows"]:
+                take = min(batch_size - n_pending, shard["n_rows"] - row)
+                pending.append(self._rows(hook, arrays, row, row + take))
+                n_pending, row = n_pending + take, row + take
+                if n_pending == batch_size:
+                    yield self._join(hook, pending)
+                    pending, n_pending = [], 0
+        if pending:
+            yield self._join(hook, pending)
+
+    def iter_batches(self, hook, batch_size, device=None):
+        """Yield `batch_size`-row batches in cache order (the last may be short), crossing
+        shard boundaries. Dense hooks yield [rows, d] tensors; encoded hooks yield CSR
+        (indptr, indices, values) tuples, which saeflow_b200.decode_sparse takes directly.
+
+        device: None yields host tensors (saeflow.cache.ActivationReader.iter_batches,
+        cache.py:178-194). A CUDA device yields tensors already there: each batch is staged
+        in pinned memory and copied asynchronously one batch ahead, so reading and the
+        copy of batch i+1 overlap the caller's work on batch i.
+        """
+        if device is None:
+            yield from self._host_batches(hook, batch_size)
+            return
+        device = torch.device(device)
+        stream = torch.cuda.Stream(device)
+
+        def upload(item):
+            ts = item if isinstance(item, tuple) else (item,)
+            with torch.cuda.stream(stream):
+                dev = tuple(t.pin_memory().to(device, non_blocking=True) for t in ts)
+                ev = torch.cuda.Event()
+                ev.record(stream)
+            return (dev if isinstance(item, tuple) else dev[0]), ev
+
+        ahead = None
+        for item in self._host_batches(hook, batch_size):
+            nxt = upload(item)
+            if ahead is not None:
+                yield self._handoff(ahead, device)
+            ahead = nxt
+        if ahead is not None:
+            yield self._handoff(ahead, device)
+
+    @staticmethod
+    def _handoff(staged, device):
+        batch, ev = staged
+        cur = torch.cuda.current_stream(device)
+        cur.wait_event(ev)
+        for t in (batch if isinstance(batch, tuple) else (batch,)):
+            t.record_stream(cur)
+        return batch

@@ -1,0 +1,195 @@
+"""Activation cache (saeflow_b200.cache), a drop-in for saeflow/cache.py.
+
+The reference's cache tests (tests/test_cache.py of saeflow) need TransformerLens, which
+is not installed; tests/cache_fixtures.TinyModel stands in for the model. Files written by
+the reference's own cache_activations with that model (tests/golden/cache_ref/, made by
+tests/golden/make_golden_cache.py) pin the format byte for byte.
+"""
+
+import filecmp
+from pathlib import Path
+
+import pytest
+import torch
+
+import cache_fixtures as cf
+import oracle
+from saeflow_b200 import cache as sf_cache
+from saeflow_b200.cache import ActivationReader, cache_activations
+from saeflow_b200.kernels import csr_to_dense
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "cache_ref"
+
+
+@pytest.fixture
+def model():
+    return cf.TinyModel()
+
+
+@pytest.fixture
+def tokens():
+    return cf.tokens()
+
+
+@pytest.fixture
+def cpu_encoder(monkeypatch):
+    """The CPU restatement of encode_sparse stands in for the CUDA kernels."""
+    monkeypatch.setattr(sf_cache, "_encode_sparse", oracle.encode_sparse)
+
+
+def read_all(reader, hook, batch_size):
+    return torch.cat(list(reader.iter_batches(hook, batch_size)))
+
+
+def same_tree(a: Path, b: Path):
+    fa = sorted(p.relative_to(a) for p in a.rglob("*") if p.is_file())
+    fb = sorted(p.relative_to(b) for p in b.rglob("*") if p.is_file())
+    assert fa == fb
+    for rel in fa:
+        assert filecmp.cmp(a / rel, b / rel, shallow=False), f"{rel} differs from the reference's file"
+
+
+# ------------------------------------------------------------------ format parity with the reference
+
+def test_dense_cache_is_byte_identical_to_the_reference(model, tokens, tmp_path):
+    cache_activations(model, tokens, cf.HOOKS, tmp_path / "dense_fp32", batch_size=4, batches_per_shard=2)
+    same_tree(tmp_path / "dense_fp32", GOLDEN / "dense_fp32")
+    cache_activations(model, tokens, cf.HOOKS[:1], tmp_path / "dense_bf16", batch_size=8, dtype=torch.bfloat16)
+    same_tree(tmp_path / "dense_bf16", GOLDEN / "dense_bf16")
+
+
+def test_encoded_cache_is_byte_identical_to_the_reference(model, tokens, tmp_path, cpu_encoder):
+    sae = cf.exact_sae(oracle.RefSAE)
+    cache_activations(model, tokens, cf.HOOKS, tmp_path / "csr_fp32", batch_size=4, batches_per_shard=2,
+                      encoders={cf.HOOKS[0]: sae})
+    same_tree(tmp_path / "csr_fp32", GOLDEN / "csr_fp32")
+
+
+def test_reader_reads_the_reference_caches(model, tokens):
+    reader = ActivationReader(GOLDEN / "dense_fp32")
+    assert reader.hook_names == cf.HOOKS and reader.n_rows() == 22 * cf.N_CTX
+    for hook in cf.HOOKS:
+        assert torch.equal(read_all(reader, hook, 7), cf.expected(model, tokens, hook))
+    got = read_all(ActivationReader(GOLDEN / "dense_bf16"), cf.HOOKS[0], 64)
+    assert got.dtype == torch.bfloat16 and torch.equal(got, cf.expected(model, tokens, cf.HOOKS[0]).bfloat16())
+    reader = ActivationReader(GOLDEN / "csr_fp32")
+    sae = cf.exact_sae(oracle.RefSAE)
+    dense = torch.cat([csr_to_dense(*csr, 96) for csr in reader.iter_batches(cf.HOOKS[0], 13)])
+    assert torch.equal(dense, sae.encode(cf.expected(model, tokens, cf.HOOKS[0])))
+
+
+# ------------------------------------------------------------------ the reference's cache tests
+
+def test_write_and_read_back_exactly(model, tokens, tmp_path):
+    cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
+    reader = ActivationReader(tmp_path)
+    assert len(reader.manifest["shards"]) == 3
+    for hook in cf.HOOKS:
+        assert torch.equal(read_all(reader, hook, 7), cf.expected(model, tokens, hook))
+
+
+def test_resume_after_interruption(model, tokens, tmp_path):
+    with pytest.raises(cf.Interrupted):
+        cache_activations(cf.FlakyModel(model, 3), tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
+    assert len(ActivationReader(tmp_path).manifest["shards"]) == 1  # the half-computed shard 1 is discarded
+    cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
+    reader = ActivationReader(tmp_path)
+    assert len(reader.manifest["shards"]) == 3
+    assert not list(tmp_path.rglob("*.tmp"))
+    for hook in cf.HOOKS:
+        assert torch.equal(read_all(reader, hook, 5), cf.expected(model, tokens, hook))
+
+
+def test_resume_with_different_config_refuses(model, tokens, tmp_path):
+    cache_activations(model, tokens, cf.HOOKS[:1], tmp_path, batch_size=4)
+    with pytest.raises(ValueError, match="different config"):
+        cache_activations(model, tokens, cf.HOOKS[:1], tmp_path, batch_size=8)
+
+
+def test_encoders_for_uncached_hooks_refused(model, tokens, tmp_path):
+    with pytest.raises(ValueError, match="not being cached"):
+        cache_activations(model, tokens, cf.HOOKS[:1], tmp_path, encoders={cf.HOOKS[1]: object()})
+
+
+def test_bfloat16_storage(model, tokens, tmp_path):
+    hook = cf.HOOKS[0]
+    cache_activations(model, tokens, [hook], tmp_path, batch_size=8, dtype=torch.bfloat16)
+    got = read_all(ActivationReader(tmp_path), hook, 64)
+    assert got.dtype == torch.bfloat16
+    assert torch.equal(got, cf.expected(model, tokens, hook).bfloat16())
+
+
+def test_encode_on_the_fly_stores_sparse(model, tokens, tmp_path, cpu_encoder):
+    hook = cf.HOOKS[0]
+    sae = cf.exact_sae(oracle.RefSAE)
+    cache_activations(model, tokens, [hook], tmp_path, batch_size=4, batches_per_shard=2, encoders={hook: sae})
+    reader = ActivationReader(tmp_path)
+    assert reader.manifest["hooks"][hook] == {"format": "csr", "d": 96}
+    dense = torch.cat([csr_to_dense(*csr, 96) for csr in reader.iter_batches(hook, 13)])
+    assert torch.equal(dense, sae.encode(cf.expected(model, tokens, hook)))
+
+
+# ------------------------------------------------------------------ the background writer
+
+def test_failed_shard_write_leaves_only_whole_shards_and_resumes(model, tokens, tmp_path, monkeypatch):
+    real_save, calls = sf_cache._save, []
+
+    def flaky_save(path, t):
+        calls.append(path)
+        if len(calls) == 3:  # shard 1's first file
+            raise OSError("disk full")
+        real_save(path, t)
+
+    monkeypatch.setattr(sf_cache, "_save", flaky_save)
+    with pytest.raises(RuntimeError, match="writer failed"):
+        cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
+    assert len(ActivationReader(tmp_path).manifest["shards"]) == 1
+    monkeypatch.setattr(sf_cache, "_save", real_save)
+    cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
+    same_tree(tmp_path, GOLDEN / "dense_fp32")
+
+
+def test_producer_error_still_completes_handed_over_shards(model, tokens, tmp_path):
+    # 5 forward passes: shards 0 and 1 (2 batches each) are handed to the writer, then the
+    # model dies in shard 2; both finished shards must be on disk and recorded.
+    with pytest.raises(cf.Interrupted):
+        cache_activations(cf.FlakyModel(model, 5), tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
+    assert len(ActivationReader(tmp_path).manifest["shards"]) == 2
+
+
+# ------------------------------------------------------------------ GPU: the CUDA encoder
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("sae_dtype", [torch.float32, torch.bfloat16])
+def test_cuda_encode_on_the_fly_matches_reference_files(tokens, tmp_path, sae_dtype):
+    """Model on the GPU, SAE encoded by the CUDA kernels (IEEE fp32: the dense route; bf16:
+    encode straight to CSR), D2H copies overlapped: fp32 gives the reference's files byte
+    for byte; bf16 gives the CSR of encode_sparse on the same activations."""
+    from saeflow_b200 import encode_sparse
+    from saeflow_b200.kernels import device_error
+
+    model = cf.TinyModel("cuda")
+    sae = cf.exact_sae(oracle.RefSAE).to(sae_dtype).cuda()
+    out = tmp_path / "c"
+    cache_activations(model, tokens, cf.HOOKS, out, batch_size=4, batches_per_shard=2,
+                      encoders={cf.HOOKS[0]: sae})
+    if sae_dtype == torch.float32:
+        same_tree(out, GOLDEN / "csr_fp32")
+    reader = ActivationReader(out)
+    got = torch.cat([csr_to_dense(*csr, 96) for csr in reader.iter_batches(cf.HOOKS[0], 50)])
+    acts = cf.expected(model, tokens.cuda(), cf.HOOKS[0]).to(sae_dtype)
+    want = csr_to_dense(*encode_sparse(sae, acts), 96).float().cpu()
+    assert torch.equal(got, want)
+    assert device_error() == 0
+
+
+@pytest.mark.gpu
+def test_reader_device_batches_match_host_batches(tmp_path):
+    reader = ActivationReader(GOLDEN / "csr_fp32")
+    for hook in cf.HOOKS:
+        host = list(reader.iter_batches(hook, 29))
+        dev = list(reader.iter_batches(hook, 29, device="cuda"))
+        assert len(host) == len(dev)
+        for h, d in zip(host, dev):
+            for a, b in zip(h if isinstance(h, tuple) else (h,), d if isinstance(d, tuple) else (d,)):
+                assert b.is_cuda and torch.equal(a, b.cpu())
