@@ -26,6 +26,13 @@ the host synchronously and writes each shard before computing the next
   and then the manifest, in shard order, while the next shard is computed. If the
   producer fails, the shards already handed to the writer are still completed before the
   error propagates, so the cache again holds only whole shards.
+
+Several GPUs (the reference's roadmap, README.md:234-235): with `group=` (a
+torch.distributed process group, one rank per GPU, all ranks on one filesystem) rank r
+caches a contiguous block of whole shards, writing them at their global shard numbers and
+recording them in its own manifest (`manifest.rank<r>-of-<n>.json`, so each rank resumes
+on its own); when every rank is done, rank 0 merges the rank manifests into
+`manifest.json` and removes them. The result is the directory a single process writes.
 """
 
 from __future__ import annotations
@@ -125,10 +132,12 @@ class _HostCopy:
 
 
 class _ShardWriter:
-    """One thread that assembles, writes and records shards in submission order."""
+    """One thread that assembles, writes and records shards in submission order.
+    `index_shards`: record each shard's global number (rank manifests)."""
 
-    def __init__(self, out_dir: Path, manifest: dict):
-        self.out_dir, self.manifest = out_dir, manifest
+    def __init__(self, out_dir: Path, manifest: dict, manifest_path: Path, index_shards: bool = False):
+        self.out_dir, self.manifest, self.manifest_path = out_dir, manifest, manifest_path
+        self.index_shards = index_shards
         self.jobs: queue.Queue = queue.Queue(maxsize=_WRITE_AHEAD)
         self.error: BaseException | None = None
         self.thread = threading.Thread(target=self._run, name="saeflow-cache-writer", daemon=True)
@@ -166,59 +175,36 @@ class _ShardWriter:
             else:
                 _save(self.out_dir / h / f"{shard:05d}.npy", torch.cat([c.wait() for c in pieces]))
             self.manifest["hooks"][h] = hooks_meta[h]
-        self.manifest["shards"].append({"n_seqs": n_seqs, "n_rows": n_rows})
+        entry = {"n_seqs": n_seqs, "n_rows": n_rows}
+        if self.index_shards:
+            entry["index"] = shard
+        self.manifest["shards"].append(entry)
         text = json.dumps(self.manifest, indent=2).encode()
-        _atomic_write(self.out_dir / "manifest.json", lambda fh: fh.write(text))
+        _atomic_write(self.manifest_path, lambda fh: fh.write(text))
 
 
 # ----------------------------------------------------------------------------- writer API
 
-@torch.inference_mode()
-def cache_activations(model, tokens, hook_names, out_dir, *, batch_size=8, batches_per_shard=32,
-                      dtype=torch.float32, encoders=None):
-    """Run `model` over `tokens` [n_seqs, seq_len] and cache activations at `hook_names`.
-
-    model: a TransformerLens HookedTransformer, or anything with a compatible
-      `run_with_cache(batch, names_filter=, stop_at_layer=, return_type=None)` and
-      `parameters()`.
-    encoders: optional {hook_name: sae}; those hooks are SAE-encoded on the fly on the
-      SAE's device and stored as CSR feature activations instead of dense ones.
-    Calling again with the same arguments after an interruption resumes the run.
-    Returns the cache directory as a Path. Same arguments, errors and files as
-    saeflow.cache.cache_activations (cache.py:70-137).
-    """
-    out_dir, hook_names, encoders = Path(out_dir), list(hook_names), encoders or {}
-    unknown = set(encoders) - set(hook_names)
-    if unknown:
-        raise ValueError(f"encoders given for hooks not being cached: {sorted(unknown)}")
-    config = {
-        "hook_names": hook_names,
-        "n_seqs": len(tokens),
-        "seq_len": int(tokens.shape[1]),
-        "batch_size": batch_size,
-        "batches_per_shard": batches_per_shard,
-        "dtype": str(dtype).removeprefix("torch."),
-        "encoded": sorted(encoders),
-    }
-    manifest_path = out_dir / "manifest.json"
-    if manifest_path.exists():
-        manifest = json.loads(manifest_path.read_text())
+def _load_manifest(path: Path, config: dict, out_dir: Path) -> dict:
+    if path.exists():
+        manifest = json.loads(path.read_text())
         if manifest["config"] != config:
             raise ValueError(f"{out_dir} holds a cache with a different config: {manifest['config']}")
-    else:
-        manifest = {"config": config, "hooks": {}, "shards": []}
-    for h in hook_names:
-        (out_dir / h).mkdir(parents=True, exist_ok=True)
+        return manifest
+    return {"config": config, "hooks": {}, "shards": []}
 
+
+def _run_shards(model, tokens, hook_names, out_dir, encoders, dtype, batch_size, seqs_per_shard, seq_len,
+                first, stop_shard, manifest, manifest_path, index_shards):
+    """Compute shards [first, stop_shard) and hand them to a writer that records them in
+    `manifest` / `manifest_path`."""
     device = next(model.parameters()).device
     stop = _stop_layer(hook_names)
-    seqs_per_shard = batch_size * batches_per_shard
-    first_shard = len(manifest["shards"])
     streams: dict = {}
-    writer = _ShardWriter(out_dir, manifest)
+    writer = _ShardWriter(out_dir, manifest, manifest_path, index_shards)
     try:
-        shard = first_shard
-        for start in range(first_shard * seqs_per_shard, len(tokens), seqs_per_shard):
+        for shard in range(first, stop_shard):
+            start = shard * seqs_per_shard
             end = min(start + seqs_per_shard, len(tokens))
             parts = {h: [] for h in hook_names}
             meta = {}
@@ -236,11 +222,108 @@ def cache_activations(model, tokens, hook_names, out_dir, *, batch_size=8, batch
                     else:
                         parts[h].append(_HostCopy(a.to(dtype), streams))
                         meta[h] = {"format": "dense", "d": int(a.shape[1])}
-            writer.submit((shard, parts, meta, end - start, (end - start) * config["seq_len"]))
-            shard += 1
+            writer.submit((shard, parts, meta, end - start, (end - start) * seq_len))
     finally:
         writer.close()
+
+
+@torch.inference_mode()
+def cache_activations(model, tokens, hook_names, out_dir, *, batch_size=8, batches_per_shard=32,
+                      dtype=torch.float32, encoders=None, group=None):
+    """Run `model` over `tokens` [n_seqs, seq_len] and cache activations at `hook_names`.
+
+    model: a TransformerLens HookedTransformer, or anything with a compatible
+      `run_with_cache(batch, names_filter=, stop_at_layer=, return_type=None)` and
+      `parameters()`.
+    encoders: optional {hook_name: sae}; those hooks are SAE-encoded on the fly on the
+      SAE's device and stored as CSR feature activations instead of dense ones.
+    group: optional torch.distributed process group: every rank calls with the same
+      arguments (its own model and SAEs on its own GPU) and caches its block of shards.
+    Calling again with the same arguments after an interruption resumes the run.
+    Returns the cache directory as a Path. Same arguments, errors and files as
+    saeflow.cache.cache_activations (cache.py:70-137).
+    """
+    out_dir, hook_names, encoders = Path(out_dir), list(hook_names), encoders or {}
+    unknown = set(encoders) - set(hook_names)
+    if unknown:
+        raise ValueError(f"encoders given for hooks not being cached: {sorted(unknown)}")
+    config = {
+        "hook_names": hook_names,
+        "n_seqs": len(tokens),
+        "seq_len": int(tokens.shape[1]),
+        "batch_size": batch_size,
+        "batches_per_shard": batches_per_shard,
+        "dtype": str(dtype).removeprefix("torch."),
+        "encoded": sorted(encoders),
+    }
+    seqs_per_shard = batch_size * batches_per_shard
+    n_shards = (len(tokens) + seqs_per_shard - 1) // seqs_per_shard
+    manifest_path = out_dir / "manifest.json"
+    world, rank = 1, 0
+    if group is not None:
+        import torch.distributed as dist
+
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+    manifest = _load_manifest(manifest_path, config, out_dir)
+    for h in hook_names:
+        (out_dir / h).mkdir(parents=True, exist_ok=True)
+    args = (model, tokens, hook_names, out_dir, encoders, dtype, batch_size, seqs_per_shard, config["seq_len"])
+    if world == 1:
+        _run_shards(*args, len(manifest["shards"]), n_shards, manifest, manifest_path, False)
+        return out_dir
+
+    import torch.distributed as dist
+
+    from .sharded import shard_range
+
+    done = len(manifest["shards"])  # shards a previous run (of any rank count) already merged
+    s0, s1 = shard_range(n_shards, world, rank)
+    rank_path = out_dir / f"manifest.rank{rank}-of-{world}.json"
+    rank_manifest = _load_manifest(rank_path, {**config, "rank": rank, "world": world}, out_dir)
+    if not rank_path.exists():  # recorded even when this rank's block is empty
+        text = json.dumps(rank_manifest, indent=2).encode()
+        _atomic_write(rank_path, lambda fh: fh.write(text))
+    first = max(s0, done, max((e["index"] + 1 for e in rank_manifest["shards"]), default=s0))
+    error = None
+    try:
+        _run_shards(*args, min(first, s1), s1, rank_manifest, rank_path, True)
+    except BaseException as e:  # noqa: BLE001 - every rank must reach the barrier
+        error = e
+    failed = torch.tensor([1 if error is not None else 0], dtype=torch.int32)
+    if dist.get_backend(group) == "nccl":
+        failed = failed.cuda()
+    dist.all_reduce(failed, op=dist.ReduceOp.MAX, group=group)  # also the barrier before the merge
+    if error is not None:
+        raise error
+    if int(failed.item()):
+        raise RuntimeError("another rank failed while caching; rerun with the same arguments to resume")
+    if rank == 0:
+        _merge_rank_manifests(out_dir, manifest, manifest_path, hook_names, world, done)
+    dist.barrier(group)
     return out_dir
+
+
+def _merge_rank_manifests(out_dir: Path, manifest: dict, manifest_path: Path, hook_names, world: int, done: int):
+    """Rank 0, after every rank finished: append the ranks' shards (in global order) to the
+    manifest, write it, then drop the rank manifests."""
+    paths = [out_dir / f"manifest.rank{r}-of-{world}.json" for r in range(world)]
+    entries, hooks = [], {}
+    for p in paths:
+        rm = json.loads(p.read_text())
+        entries += [e for e in rm["shards"] if e["index"] >= done]
+        hooks.update(rm["hooks"])
+    entries.sort(key=lambda e: e["index"])
+    if [e["index"] for e in entries] != list(range(done, done + len(entries))):
+        raise RuntimeError(f"rank manifests in {out_dir} do not cover consecutive shards")
+    for h in hook_names:
+        if h in hooks:
+            manifest["hooks"][h] = hooks[h]
+    manifest["hooks"] = {h: manifest["hooks"][h] for h in hook_names if h in manifest["hooks"]}
+    manifest["shards"] += [{"n_seqs": e["n_seqs"], "n_rows": e["n_rows"]} for e in entries]
+    text = json.dumps(manifest, indent=2).encode()
+    _atomic_write(manifest_path, lambda fh: fh.write(text))
+    for p in paths:
+        p.unlink()
 
 
 # ----------------------------------------------------------------------------- reader

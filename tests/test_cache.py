@@ -193,3 +193,88 @@ def test_reader_device_batches_match_host_batches(tmp_path):
         for h, d in zip(host, dev):
             for a, b in zip(h if isinstance(h, tuple) else (h,), d if isinstance(d, tuple) else (d,)):
                 assert b.is_cuda and torch.equal(a, b.cpu())
+
+
+# ------------------------------------------------------------------ several ranks (gloo, CPU)
+
+def _rank_worker(rank, world, init_file, out_dir, q, encode, flaky_rank):
+    import datetime
+    import traceback
+
+    try:
+        import torch.distributed as dist
+
+        import cache_fixtures as cfx
+        import oracle as orc
+        from saeflow_b200 import cache as c
+
+        c._encode_sparse = orc.encode_sparse
+        dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=30))
+        model = cfx.TinyModel()
+        if rank == flaky_rank:
+            model = cfx.FlakyModel(model, 1)
+        enc = {cfx.HOOKS[0]: cfx.exact_sae(orc.RefSAE)} if encode else None
+        try:
+            c.cache_activations(model, cfx.tokens(), cfx.HOOKS, out_dir, batch_size=4, batches_per_shard=2,
+                                encoders=enc, group=dist.group.WORLD)
+            q.put((rank, "ok", ""))
+        except Exception as e:  # noqa: BLE001
+            q.put((rank, "raised", type(e).__name__))
+        dist.destroy_process_group()
+    except Exception:  # noqa: BLE001
+        q.put((rank, "error", traceback.format_exc()))
+
+
+def _run_ranks(world, out_dir, encode=False, flaky_rank=-1, timeout=120):
+    import multiprocessing as mp
+    import os
+    import time
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    init_file = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"sf_cache_{os.getpid()}_{time.time_ns()}")
+    procs = [ctx.Process(target=_rank_worker, args=(r, world, init_file, str(out_dir), q, encode, flaky_rank))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    out, deadline = {}, time.time() + timeout
+    while len(out) < world and time.time() < deadline:
+        try:
+            item = q.get(timeout=max(0.1, deadline - time.time()))
+            out[item[0]] = item
+        except Exception:  # noqa: BLE001
+            break
+    for p in procs:
+        p.join(timeout=10)
+        if p.is_alive():
+            p.kill()
+    try:
+        os.remove(init_file)
+    except OSError:
+        pass
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("encode", [False, True])
+def test_ranks_write_the_single_process_cache(tmp_path, world, encode):
+    """Each rank caches its block of whole shards; after the merge the directory is the one a
+    single process writes (byte for byte, against the reference's files). With 4 ranks and 3
+    shards one rank has nothing to do."""
+    out = _run_ranks(world, tmp_path / "c", encode=encode)
+    assert sorted(out) == list(range(world)), out
+    assert all(v[1] == "ok" for v in out.values()), out
+    ref = GOLDEN / ("csr_fp32" if encode else "dense_fp32")
+    same_tree(tmp_path / "c", ref)
+
+
+def test_rank_failure_is_reported_everywhere_and_resumes(tmp_path):
+    out = _run_ranks(2, tmp_path / "c", flaky_rank=1)  # rank 1 dies after one forward pass
+    assert sorted(out) == [0, 1], out
+    assert out[1][1] == "raised" and out[1][2] == "Interrupted"
+    assert out[0][1] == "raised" and out[0][2] == "RuntimeError"
+    assert not (tmp_path / "c" / "manifest.json").exists()  # nothing merged
+    out = _run_ranks(2, tmp_path / "c")
+    assert all(v[1] == "ok" for v in out.values()), out
+    same_tree(tmp_path / "c", GOLDEN / "dense_fp32")
