@@ -302,6 +302,7 @@ def run_ours(args, rank, world, device):
         sae = make_sae(cfg_id, device)
     flush = torch.zeros(64 << 20, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
+    quads = 0  # CSR route: CUDA-event quads per step (start, encoded, CSR placed, decoded), one per chunk
 
     if sharded is not None:
         n_chunks = (T + args.chunk_tokens - 1) // args.chunk_tokens
@@ -357,30 +358,42 @@ def run_ours(args, rank, world, device):
         if cfg_id != 5:
             x = make_tokens(cfg_id, rank, device, T)
 
-        # What saeflow_b200.forward runs: the CSR stays on the device (no host sync mid-step).
-        def step(ev):
-            ev[0].record(stream)
-            h = encode_csr_stage(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation,
-                                 device_consumer=True)
-            ev[1].record(stream)
-            indptr, indices, values, overflow = encode_csr_finish_async(h)
-            ev[2].record(stream)
-            out = sparse_decode(indptr, indices, values, sae.W_dec, sae.b_dec)
-            ev[3].record(stream)
-            step.checks.append((indptr[-1], overflow))
-            return out
+        # What saeflow_b200.forward runs: the CSR stays on the device (no host sync mid-step),
+        # batches above FORWARD_CHUNK_ROWS rows as consecutive chunks into one output.
+        from saeflow_b200.ops import FORWARD_CHUNK_ROWS
+
+        chunks = [(r0, min(T, r0 + FORWARD_CHUNK_ROWS)) for r0 in range(0, T, FORWARD_CHUNK_ROWS)]
+        quads = len(chunks)
+        out_buf = torch.empty(T, c["d_in"], dtype=c["dtype"], device=device)
+
+        def step(evs):
+            for ev, (r0, r1) in zip(evs, chunks):
+                ev[0].record(stream)
+                h = encode_csr_stage(x[r0:r1], sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation,
+                                     device_consumer=True)
+                ev[1].record(stream)
+                indptr, indices, values, overflow = encode_csr_finish_async(h)
+                ev[2].record(stream)
+                sparse_decode(indptr, indices, values, sae.W_dec, sae.b_dec, out=out_buf[r0:r1])
+                ev[3].record(stream)
+                step.checks.append((indptr[-1], overflow))
+            return out_buf
         step.checks = []
-        launches_per_step = 5  # shift, encode+stage, indptr scan, place, decode
+        launches_per_step = 5 * quads  # per chunk: shift, encode+stage, indptr scan, place, decode
 
     def barrier():
         if world > 1:
             torch.distributed.barrier()
         torch.cuda.synchronize(device)
 
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    def new_quads():
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(max(quads, 1))]
+        return evs if quads else evs[0]
+
+    events = [new_quads() for _ in range(args.steps)]
     for _ in range(args.warmup):
         l2_flush(flush)
-        step([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+        step(new_quads())
     barrier()
     with ClockSampler(device.index) as clk:
         barrier()
@@ -394,13 +407,18 @@ def run_ours(args, rank, world, device):
         nnz_ovf = torch.stack([torch.stack([a, b.to(torch.int64)]) for a, b in step.checks]).cpu()
         if int(nnz_ovf[:, 1].max()):
             raise RuntimeError("CSR staging overflowed inside the timed region: the step did not do the work")
-        step.nnz = int(nnz_ovf[-1, 0])
+        step.nnz = int(nnz_ovf[-quads:, 0].sum())  # the last step's chunks
         step.checks.clear()
-    step_ms = [e[0].elapsed_time(e[3]) for e in events]
     staged = cfg_id != 3 and sharded is None  # stage events recorded
-    enc_ms = [e[0].elapsed_time(e[1]) for e in events] if staged else []
-    csr_ms = [e[1].elapsed_time(e[2]) for e in events] if cfg_id in (1, 2, 5) and staged else []
-    dec_ms = [e[2].elapsed_time(e[3]) for e in events] if staged else (step_ms if cfg_id == 3 else [])
+    if quads:  # one event quad per forward chunk: stage times summed over the chunks
+        step_ms = [e[0][0].elapsed_time(e[-1][3]) for e in events]
+        stage_ms = [[sum(q[j].elapsed_time(q[j + 1]) for q in e) for j in range(3)] for e in events]
+    else:
+        step_ms = [e[0].elapsed_time(e[3]) for e in events]
+        stage_ms = [[e[j].elapsed_time(e[j + 1]) for j in range(3)] for e in events] if staged else []
+    enc_ms = [st[0] for st in stage_ms]
+    csr_ms = [st[1] for st in stage_ms] if cfg_id in (1, 2, 5) else []
+    dec_ms = [st[2] for st in stage_ms] if staged else (step_ms if cfg_id == 3 else [])
     total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
     if world > 1:
         torch.distributed.all_reduce(total_ms, op=torch.distributed.ReduceOp.MAX)

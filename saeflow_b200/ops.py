@@ -65,16 +65,38 @@ def _forward_async(sae, x, out=None, *, add_b_dec=True, out_dtype=None):
     return sparse_decode(*csr, sae.W_dec, b_dec, out=out, out_dtype=out_dtype), overflow
 
 
+# Rows per encode launch of forward(): larger batches run as consecutive launches of this
+# size. It bounds the CSR staging (M x d_sae/256 tile counts) and, measured on B200 at
+# d_sae = 2^20, keeps the power-capped SM clock higher than one launch over every row
+# (1327 MHz at 16384 rows per launch against 960 MHz at 262144).
+FORWARD_CHUNK_ROWS = 16384
+
+
 def forward(sae, x):
     """encode_sparse then decode_sparse: the dense features never reach the decoder (ops.py:47-49).
 
     The CSR stays on the device between the two, so nothing waits on the host between the
     encoder and the decoder; the one host read (as in the reference, decode.py:88) comes at
-    the end and checks that the CSR staging did not overflow (it then redoes the batch
-    through encode_sparse's exact-size route)."""
-    out, overflow = _forward_async(sae, x)
-    if overflow is not None and int(overflow):
-        out = decode_sparse(sae, encode_sparse(sae, x))
+    the end and checks that the CSR staging did not overflow (a chunk that overflowed is
+    redone through encode_sparse's exact-size route). Batches above FORWARD_CHUNK_ROWS rows
+    run as consecutive chunks into one output."""
+    M = x.shape[0]
+    if M <= FORWARD_CHUNK_ROWS:
+        out, overflow = _forward_async(sae, x)
+        if overflow is not None and int(overflow):
+            out = decode_sparse(sae, encode_sparse(sae, x))
+        return out
+    out = torch.empty(M, sae.W_dec.shape[1], dtype=sae.W_dec.dtype, device=x.device)
+    flags = []
+    for r0 in range(0, M, FORWARD_CHUNK_ROWS):
+        r1 = min(M, r0 + FORWARD_CHUNK_ROWS)
+        _, overflow = _forward_async(sae, x[r0:r1], out[r0:r1])
+        if overflow is not None:
+            flags.append((r0, r1, overflow))
+    bad = torch.stack([f for _, _, f in flags]).tolist() if flags else []
+    for (r0, r1, _), ovf in zip(flags, bad):
+        if ovf:
+            out[r0:r1] = decode_sparse(sae, encode_sparse(sae, x[r0:r1]))
     return out
 
 
@@ -89,14 +111,30 @@ def _streams(dev):
         return _copy_streams[dev]
 
 
+def _chunk_plan(M, C):
+    """Row counts of forward_host's chunks: a ramp of C/4 and C/2 at both ends around full
+    chunks of at most C, so the first host-to-device copy and the last device-to-host copy,
+    which nothing overlaps, move a quarter chunk each."""
+    if M <= C:
+        return [M]
+    ramp = [max(1, C // 4), max(1, C // 2)]
+    mid = M - 2 * sum(ramp)
+    if mid <= 0:
+        n = -(-M // C)
+        return [M // n + (1 if i < M % n else 0) for i in range(n)]
+    n = -(-mid // C)
+    return ramp + [mid // n + (1 if i < mid % n else 0) for i in range(n)] + ramp[::-1]
+
+
 def forward_host(sae, x, out=None, *, chunk_tokens=4096):
     """forward() for a batch held in host memory, returning host memory.
 
     x: [M, d_in] CPU tensor (pinned for the copies to overlap; pageable x is pinned first).
     out: optional [M, d_in] pinned CPU tensor of W_dec's dtype to write into.
-    The batch runs in chunks of `chunk_tokens` rows on sae's device: chunk i+1's host-to-device
-    copy and chunk i-1's device-to-host copy run on their own streams while chunk i is encoded
-    and decoded on the current stream, with two device buffers per direction. One host sync at
+    The batch runs in chunks of at most `chunk_tokens` rows on sae's device (quarter and half
+    chunks at both ends): chunk i+1's host-to-device copy and chunk i-1's device-to-host copy
+    run on their own streams while chunk i is encoded and decoded on the current stream, with
+    two device buffers per direction. One host sync at
     the end waits for the last copy and reads every chunk's overflow flag; a chunk whose CSR
     staging overflowed is redone through forward().
     """
@@ -120,14 +158,16 @@ def forward_host(sae, x, out=None, *, chunk_tokens=4096):
         x = x.pin_memory()
     compute = torch.cuda.current_stream(dev)
     h2d, d2h = _streams(dev)
-    C = min(chunk_tokens, M)
+    plan = _chunk_plan(M, chunk_tokens)
+    C = max(plan)
     xbuf = [torch.empty(C, x.shape[1], dtype=x.dtype, device=dev) for _ in range(2)]
     obuf = [torch.empty(C, D, dtype=dt, device=dev) for _ in range(2)]
     ev_in, ev_done, ev_out = [], [], []
     flags = []
-    for i, r0 in enumerate(range(0, M, C)):
-        r1 = min(M, r0 + C)
-        n, s = r1 - r0, i % 2
+    r1 = 0
+    for i, n in enumerate(plan):
+        r0, r1 = r1, r1 + n
+        s = i % 2
         ev_in.append(torch.cuda.Event())
         ev_done.append(torch.cuda.Event())
         ev_out.append(torch.cuda.Event())

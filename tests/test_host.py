@@ -1,0 +1,16 @@
+"""Host-side scheduling logic that needs no GPU."""
+
+import pytest
+
+from saeflow_b200.ops import _chunk_plan
+
+
+@pytest.mark.parametrize("M,C", [(16384, 4096), (16384, 2048), (1500, 64), (1500, 1000), (1500, 5000),
+                                 (5000, 4096), (10, 4), (3, 1), (100, 1), (1, 4096), (12288, 4096)])
+def test_forward_host_chunk_plan(M, C):
+    plan = _chunk_plan(M, C)
+    assert sum(plan) == M and min(plan) >= 1 and max(plan) <= C
+    if M > 3 * C:
+        # quarter and half chunks at both ends shorten the copies nothing overlaps
+        ramp = [max(1, C // 4), max(1, C // 2)]
+        assert plan[:2] == ramp and plan[-2:] == ramp[::-1]

@@ -355,7 +355,12 @@ def test_forward_host_matches_forward(activation, chunk):
     M, d_in, d_sae = 1500, 256, 4099
     sae = _sparse_sae(d_in, d_sae, activation, k=16 if activation == "topk" else None)
     x = torch.randn(M, d_in).to(torch.bfloat16)
-    want = torch.cat([forward(sae, x[r0:r0 + chunk].cuda()).cpu() for r0 in range(0, M, chunk)])
+    from saeflow_b200.ops import _chunk_plan
+
+    bounds = [0]
+    for n in _chunk_plan(M, chunk):
+        bounds.append(bounds[-1] + n)
+    want = torch.cat([forward(sae, x[a:b].cuda()).cpu() for a, b in zip(bounds, bounds[1:])])
     whole = forward(sae, x.cuda()).cpu()
     got = forward_host(sae, x.pin_memory(), chunk_tokens=chunk)
     torch.testing.assert_close(got.float(), whole.float(), atol=0.1, rtol=TOL[torch.bfloat16])
