@@ -30,6 +30,7 @@
 // shift_convert_kernel: a separate HBM pass costs <1% of the GEMM, whereas shifting in
 // shared memory would compete with the tensor cores for shared-memory bandwidth.
 #include <algorithm>
+#include <cstddef>
 #include <mutex>
 
 #include <cudaTypedefs.h>
@@ -95,7 +96,8 @@ struct TcParams {
     unsigned stage_cap;
 };
 
-struct __align__(8) TcShared {
+// The staged bias / cut arrays are read as float4: they must start on 16-byte boundaries.
+struct __align__(16) TcShared {
     uint64_t full[8];
     uint64_t empty[8];
     uint64_t tmem_full[2];
@@ -103,9 +105,10 @@ struct __align__(8) TcShared {
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
-    float bias[2][kBN];
-    float thr[2][kBN];
+    alignas(16) float bias[2][kBN];
+    alignas(16) float thr[2][kBN];
 };
+static_assert(offsetof(TcShared, bias) % 16 == 0 && offsetof(TcShared, thr) % 16 == 0, "float4 staging");
 
 // Unit u -> (m_blk, first n_blk, n-tile count).
 struct Unit {
