@@ -1,19 +1,25 @@
 """Benchmark of the SAE hot path (encode -> CSR -> decode) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-triton]
+                    [--config 1..5] [--partition token|feature] [--route csr|dense]
 
-One step = one forward pass (fused encode with row counts -> dense_to_csr -> sparse
-decode) over one batch of synthetic tokens. Default workload: BASELINE config 2,
-JumpReLU SAE d_in=2304 d_sae=65536 bf16, 16384 tokens per GPU, inputs generated with
-that config's distributions (seeded; the reference benchmarks on synthetic data too).
+One step = one forward pass over one batch of synthetic tokens, as saeflow_b200.forward
+runs it: the encoder GEMM writing CSR straight from its epilogue, the sync-free indptr scan
+and placement, the CSR decode. Default workload: BASELINE config 2, JumpReLU SAE d_in=2304
+d_sae=65536 bf16, 16384 tokens per GPU, inputs generated with that config's distributions
+(seeded; the reference benchmarks on synthetic data too). `e2e` times
+saeflow_b200.forward_host on pinned host tokens (copies inside the timed region).
 
 Multi-GPU (torchrun, one process per GPU, NCCL): token-sharded with replicated weights,
 per-GPU work fixed ("weak" scaling), no collective on the data path; the timed region
-is bracketed by a barrier + synchronize and the max over ranks is reported.
+is bracketed by a barrier + synchronize and the max over ranks is reported. Config 5 is
+strong scaling over a fixed 262144-token job, token- or feature-sharded.
 
---impl reference times the reference's own CPU implementation of the path (the CPU
+--impl reference times the reference's CPU implementation of the path (the CPU
 restatement in oracle/: dense torch SAE encode -> to_sparse_csr -> CSR addmm, as the
 reference's bench does) on the host cores, on a bounded token sample per step.
+--impl reference-triton times the reference's own GPU path (saeflow.forward and its Triton
+kernels, installed unmodified in baseline/_ref) on one GPU with this arm's inputs.
 """
 
 from __future__ import annotations
@@ -608,6 +614,60 @@ def cpu_baseline(cfg_id, budget_s=10.0, sample_tokens=None):
                       "(oracle restatement of the reference CPU path: dense encode -> to_sparse_csr -> addmm)"}
 
 
+def run_reference_triton(args, device):
+    """The reference's own GPU path (saeflow.forward with its Triton kernels, installed
+    unmodified in baseline/_ref) on the same config, inputs and timing as our arm."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "saeflow").is_dir():
+        return {"impl": "reference-triton", "unavailable": "baseline/_ref does not hold the reference package"}
+    sys.path.insert(0, str(ref_dir))
+    import saeflow
+
+    cfg_id = args.config
+    if cfg_id not in (1, 2, 4):
+        return {"impl": "reference-triton", "unavailable": f"config {cfg_id} has no forward pass to time"}
+    c = CONFIGS[cfg_id]
+    T = args.tokens or c["tokens"]
+    sae = make_sae(cfg_id, device)
+    x = make_tokens(cfg_id, 0, device, T)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(fn, steps):
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(steps)]
+        for ev in evs:
+            l2_flush(flush)
+            ev[0].record(stream)
+            fn()
+            ev[1].record(stream)
+        torch.cuda.synchronize(device)
+        return sum(e[0].elapsed_time(e[1]) for e in evs)
+
+    for _ in range(args.warmup):  # includes the reference's Triton autotuning
+        l2_flush(flush)
+        saeflow.forward(sae, x)
+    with ClockSampler(device.index) as clk:
+        total = timed(lambda: saeflow.forward(sae, x), args.steps)
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(T, c["d_in"], dtype=c["dtype"]).pin_memory()
+    e_total = timed(lambda: out_host.copy_(saeflow.forward(sae, x_host.to(device, non_blocking=True)),
+                                           non_blocking=True), args.steps)
+    nbytes = T * c["d_in"] * x.element_size()
+    return {
+        "metric": METRIC, "value": round(T * args.steps / (total / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if c["dtype"] == torch.bfloat16 else "fp32", "data": "synthetic (seeded)",
+        "config": {"workload": c["name"], "tokens_per_gpu": T,
+                   "l2": "flushed between steps (256 MB write, outside the per-step events)"},
+        "impl": "reference-triton",
+        "api": "saeflow.forward(sae, x) from baseline/_ref (the reference's Triton kernels, unmodified)",
+        "e2e": {"value": round(T * args.steps / (e_total / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes},
+        "clocks": clk.summary(),
+    }
+
+
 def run_reference(args):
     cfg_id = args.config
     c = CONFIGS[cfg_id]
@@ -643,7 +703,9 @@ def main(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours",
+                    help="reference: the reference's CPU path (the driver's reference arm); reference-triton: "
+                         "the reference's own GPU kernels from baseline/_ref, one GPU")
     ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=2)
     ap.add_argument("--tokens", type=int, default=None, help="tokens per GPU (default: the config's)")
     ap.add_argument("--cpu-tokens", type=int, default=1024, help="reference arm: tokens per step")
@@ -666,6 +728,12 @@ def main(argv=None):
     if args.impl == "reference":
         if rank == 0:
             print(json.dumps(run_reference(args)), flush=True)
+        return 0
+    if args.impl == "reference-triton":
+        if rank == 0:
+            device = torch.device("cuda", local_rank)
+            torch.cuda.set_device(device)
+            print(json.dumps(run_reference_triton(args, device)), flush=True)
         return 0
 
     device = torch.device("cuda", local_rank)

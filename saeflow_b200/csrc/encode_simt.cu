@@ -4,9 +4,12 @@
 // allowed (saeflow/kernels/encode.py:118-120); this kernel is that path. Epilogue
 // semantics are identical to the tensor-core kernel (encode.py:195-208).
 //
-// 128 x 128 output tile per CTA, K in steps of 8 through double-buffered shared memory,
-// 256 threads each owning an 8 x 8 register block (rows {4ty..4ty+3, 64+4ty..}, columns
-// {4tx..4tx+3, 64+4tx..}) so the shared-memory reads are conflict-free float4 broadcasts.
+// 128 x (64*NF) output tile per CTA, K in steps of 8 through double-buffered shared memory,
+// 256 threads each owning an 8 x (4*NF) register block (rows {4ty..4ty+3, 64+4ty..}, columns
+// {64q+4tx..64q+4tx+3 : q < NF}) so the shared-memory reads are conflict-free float4
+// broadcasts. NF=4 (128 x 256 tiles, 128 accumulators per thread) is the default: per K step
+// a thread issues 6 shared loads for 128 FMAs (4 for 64 with NF=2), which moved the FMA pipe
+// from 62% busy (instruction-issue bound) toward its peak; NF=2 serves d_sae < 256.
 #include "sf_common.cuh"
 #include "sf_internal.h"
 
@@ -14,7 +17,7 @@ namespace sf {
 
 namespace {
 
-constexpr int SB_M = 128, SB_N = 128, SB_K = 8, SB_T = 256;
+constexpr int SB_M = 128, SB_K = 8, SB_T = 256;
 
 template <typename OT>
 __device__ __forceinline__ void simt_store4(void *out, int64_t sm, int64_t sn, int vec, int64_t N, int row, int col,
@@ -37,9 +40,12 @@ __device__ __forceinline__ void simt_store4(void *out, int64_t sm, int64_t sn, i
         if (col + j < N) base[(int64_t)(col + j) * sn] = from_f32<OT>(v[j]);
 }
 
-__global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restrict__ xs, int64_t ldx,
-                                                          const float *__restrict__ W, int64_t swk, int64_t swn,
-                                                          int M, int N, int K, EpilogueArgs ep, int w_vec) {
+template <int NF>
+__global__ void __launch_bounds__(SB_T, NF == 2 ? 2 : 1)
+    encode_simt_kernel(const float *__restrict__ xs, int64_t ldx, const float *__restrict__ W, int64_t swk,
+                       int64_t swn, int M, int N, int K, EpilogueArgs ep, int w_vec) {
+    constexpr int SB_N = 64 * NF;
+    constexpr int BQ = NF / 2;  // float4 loads of the B tile per thread per K step
     __shared__ __align__(16) float As[2][SB_K][SB_M + 4];
     __shared__ __align__(16) float Bs[2][SB_K][SB_N + 4];
     __shared__ float s_bias[SB_N], s_thr[SB_N];
@@ -56,11 +62,12 @@ __global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restri
                        : 0.f;
     }
 
-    // Global -> register staging: A: row = tid/2, k-quad = tid%2; B: k = tid/32, n-quad = tid%32.
+    // Global -> register staging: A: row = tid/2, k-quad = tid%2; B: k = tid/32, n-quads
+    // (tid%32)*4 + 128q.
     const int a_row = tid >> 1, a_kq = (tid & 1) * 4;
     const int b_k = tid >> 5, b_nq = (tid & 31) * 4;
     float4 ra;
-    float rb[4];
+    float rb[BQ][4];
 
     auto load_tile = [&](int k0) {
         const int gr = m0 + a_row, gk = k0 + a_kq;
@@ -68,14 +75,17 @@ __global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restri
         ra = (gr < M && gk < K) ? *reinterpret_cast<const float4 *>(xs + (int64_t)gr * ldx + gk)
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
         const int kk = k0 + b_k;
-        const int nn = n0 + b_nq;
-        if (w_vec && kk < K && nn + 4 <= N) {
-            const float4 t = *reinterpret_cast<const float4 *>(W + (int64_t)kk * swk + nn);
-            rb[0] = t.x, rb[1] = t.y, rb[2] = t.z, rb[3] = t.w;
-        } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                rb[j] = (kk < K && nn + j < N) ? __ldg(W + (int64_t)kk * swk + (int64_t)(nn + j) * swn) : 0.f;
+        for (int q = 0; q < BQ; ++q) {
+            const int nn = n0 + b_nq + q * 128;
+            if (w_vec && kk < K && nn + 4 <= N) {
+                const float4 t = *reinterpret_cast<const float4 *>(W + (int64_t)kk * swk + nn);
+                rb[q][0] = t.x, rb[q][1] = t.y, rb[q][2] = t.z, rb[q][3] = t.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    rb[q][j] = (kk < K && nn + j < N) ? __ldg(W + (int64_t)kk * swk + (int64_t)(nn + j) * swn) : 0.f;
+            }
         }
     };
     auto store_tile = [&](int buf) {
@@ -83,14 +93,17 @@ __global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restri
         As[buf][a_kq + 1][a_row] = ra.y;
         As[buf][a_kq + 2][a_row] = ra.z;
         As[buf][a_kq + 3][a_row] = ra.w;
-        *reinterpret_cast<float4 *>(&Bs[buf][b_k][b_nq]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+#pragma unroll
+        for (int q = 0; q < BQ; ++q)
+            *reinterpret_cast<float4 *>(&Bs[buf][b_k][b_nq + q * 128]) =
+                make_float4(rb[q][0], rb[q][1], rb[q][2], rb[q][3]);
     };
 
-    float acc[8][8];
+    float acc[8][4 * NF];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < 4 * NF; ++j) acc[i][j] = 0.f;
 
     const int nk = (K + SB_K - 1) / SB_K;
     load_tile(0);
@@ -103,14 +116,17 @@ __global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restri
         for (int kk = 0; kk < SB_K; ++kk) {
             const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
             const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);
-            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][tx * 4]);
-            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][kk][64 + tx * 4]);
             const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-            const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+            float b[4 * NF];
+#pragma unroll
+            for (int q = 0; q < NF; ++q) {
+                const float4 bq = *reinterpret_cast<const float4 *>(&Bs[buf][kk][q * 64 + tx * 4]);
+                b[4 * q + 0] = bq.x, b[4 * q + 1] = bq.y, b[4 * q + 2] = bq.z, b[4 * q + 3] = bq.w;
+            }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+                for (int j = 0; j < 4 * NF; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
         }
         if (kt + 1 < nk) store_tile(buf ^ 1);
         __syncthreads();
@@ -123,7 +139,7 @@ __global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restri
         const int row = m0 + r;
         int cnt = 0;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+        for (int h = 0; h < NF; ++h) {
             const int c = h * 64 + tx * 4;
             float v[4];
 #pragma unroll
@@ -155,11 +171,16 @@ __global__ void __launch_bounds__(SB_T) encode_simt_kernel(const float *__restri
 
 int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
                     int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream) {
-    if ((N + SB_N - 1) / SB_N > 2147483647ll || (M + SB_M - 1) / SB_M > 65535)
+    const bool wide = N >= 256;
+    const int64_t sb_n = wide ? 256 : 128;
+    if ((N + sb_n - 1) / sb_n > 2147483647ll || (M + SB_M - 1) / SB_M > 65535)
         return set_error(SF_ERR_UNSUPPORTED, "SIMT encode grid too large (M=%lld N=%lld)", (long long)M, (long long)N);
     const int w_vec = (swn == 1 && (swk % 4) == 0 && (reinterpret_cast<uintptr_t>(W) & 15u) == 0) ? 1 : 0;
-    dim3 grid((unsigned)((N + SB_N - 1) / SB_N), (unsigned)((M + SB_M - 1) / SB_M));
-    encode_simt_kernel<<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec);
+    dim3 grid((unsigned)((N + sb_n - 1) / sb_n), (unsigned)((M + SB_M - 1) / SB_M));
+    if (wide)
+        encode_simt_kernel<4><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec);
+    else
+        encode_simt_kernel<2><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec);
     return check_cuda(cudaGetLastError(), "encode_simt launch");
 }
 
