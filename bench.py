@@ -712,7 +712,7 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-chunk", type=int, default=4096, help="forward_host chunk size (tokens)")
+    ap.add_argument("--e2e-chunk", type=int, default=8192, help="forward_host chunk size (tokens)")
     ap.add_argument("--partition", choices=["token", "feature"], default="token",
                     help="config 5: token-sharded (weights replicated) or feature-sharded (d_sae split)")
     ap.add_argument("--chunk-tokens", type=int, default=16384,

@@ -126,7 +126,7 @@ def _chunk_plan(M, C):
     return ramp + [mid // n + (1 if i < mid % n else 0) for i in range(n)] + ramp[::-1]
 
 
-def forward_host(sae, x, out=None, *, chunk_tokens=4096):
+def forward_host(sae, x, out=None, *, chunk_tokens=8192):
     """forward() for a batch held in host memory, returning host memory.
 
     x: [M, d_in] CPU tensor (pinned for the copies to overlap; pageable x is pinned first).
