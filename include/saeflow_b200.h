@@ -235,6 +235,47 @@ SF_API int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_v
                    int values_dtype, int allow_tf32, void *workspace, size_t workspace_bytes,
                    sf_stream stream);
 
+/* ------------------------------------------------------------------------------------
+ * Backward of the sparse forward (training on sparse features). The reference has no
+ * backward kernels; these implement its roadmap item (README.md:244). With the forward
+ * f = act((x - b_dec) @ W_enc + b_enc) as CSR and x_hat = f @ W_dec + b_dec, and
+ * g = dL/dx_hat: dpre = sf_csr_sddmm(g, W_dec) on the CSR pattern, dW_dec and dW_enc^T /
+ * db_enc from sf_csc_accumulate over the transposed pattern, dx from sf_sparse_decode of
+ * dpre against W_enc^T.
+ */
+
+/* Bytes of workspace sf_csr_transpose needs for n_cols columns. */
+SF_API int sf_csr_transpose_workspace(int64_t n_cols, size_t *bytes);
+
+/*
+ * Column view of a CSR pattern: col_ptr int64 [n_cols+1], and for each column's entries
+ * (rows ascending only in expectation: the order within a column is not fixed)
+ * row_idx int32 [nnz] (the entry's row) and perm int64 [nnz] (its position in the CSR).
+ * An index outside [0, n_cols) is skipped and sets bit 2 of the device error.
+ */
+SF_API int sf_csr_transpose(const int64_t *indptr, int64_t M, const int32_t *indices, int64_t nnz, int64_t n_cols,
+                            int64_t *col_ptr, int32_t *row_idx, int64_t *perm, void *workspace,
+                            size_t workspace_bytes, sf_stream stream);
+
+/*
+ * Sampled dot products on a CSR pattern:
+ *   out[e] = (values[e] != 0) * sum_d G[row(e), d] * W[indices[e], d]      (fp32 accumulation)
+ * G [M, D] and W [n, D] of one dtype with unit column stride; values (values_dtype) masks
+ * entries whose forward value is zero (TopK's non-positive picks).
+ */
+SF_API int sf_csr_sddmm(const int64_t *indptr, int64_t M, const int32_t *indices, const sf_matrix *G,
+                        const sf_matrix *W, const void *values, int values_dtype, float *out, sf_stream stream);
+
+/*
+ * Per-column gather-accumulate over the column view of sf_csr_transpose:
+ *   out[j, :] = sum_{p in column j} values[perm[p]] * R[row_idx[p], :]     (fp64 accumulation)
+ *   col_sums[j] = sum_{p in column j} values[perm[p]]                      (optional, may be NULL)
+ * out is fp32 [n_cols, R.cols] with row pitch ld_out; R has unit column stride.
+ */
+SF_API int sf_csc_accumulate(const int64_t *col_ptr, int64_t n_cols, const int32_t *row_idx, const int64_t *perm,
+                             const void *values, int values_dtype, const sf_matrix *R, float *out, int64_t ld_out,
+                             float *col_sums, sf_stream stream);
+
 #ifdef __cplusplus
 }
 #endif
