@@ -310,7 +310,30 @@ def run_ours(args, rank, world, device):
     stream = torch.cuda.current_stream(device)
     quads = 0  # CSR route: CUDA-event quads per step (start, encoded, CSR placed, decoded), one per chunk
 
-    if sharded is not None:
+    if args.train:
+        # A training step on sparse features: the autograd forward and its backward kernels.
+        from saeflow_b200 import training
+
+        if cfg_id not in (1, 2, 4):
+            raise SystemExit("--train runs configs 1, 2 and 4")
+        x = make_tokens(cfg_id, rank, device, T)
+        for name in ("W_enc", "b_enc", "W_dec", "b_dec"):
+            getattr(sae, name).requires_grad_(True)
+        grad_out = (torch.randn(T, c["d_in"], generator=torch.Generator(device=device).manual_seed(7),
+                                device=device) * 1e-2).to(c["dtype"])
+
+        def step(ev):
+            ev[0].record(stream)
+            out = training.forward(sae, x)
+            ev[1].record(stream)
+            ev[2].record(stream)
+            torch.autograd.backward(out, grad_out)
+            ev[3].record(stream)
+            for name in ("W_enc", "b_enc", "W_dec", "b_dec"):
+                getattr(sae, name).grad = None
+            return out
+        launches_per_step = 12  # forward 5 (4 for TopK) + sddmm, count, scan, scatter, 2 accumulates, decode
+    elif sharded is not None:
         n_chunks = (T + args.chunk_tokens - 1) // args.chunk_tokens
 
         def step(ev):
@@ -432,7 +455,7 @@ def run_ours(args, rank, world, device):
 
     # ---- end to end through the public API with host buffers (H2D in, D2H out, per step)
     e2e = None
-    if cfg_id in (1, 2, 4, 5) and not args.no_e2e:
+    if cfg_id in (1, 2, 4, 5) and not args.no_e2e and not args.train:
         x_host = x.cpu().pin_memory()
         out_host = torch.empty(T, c["d_in"], dtype=c["dtype"]).pin_memory()
         e_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
@@ -477,7 +500,16 @@ def run_ours(args, rank, world, device):
     e = c["dtype"].itemsize if hasattr(c["dtype"], "itemsize") else torch.finfo(c["dtype"]).bits // 8
     stages = {}
     roofline = None
-    if sharded is not None:
+    if args.train:
+        # Forward (encode + CSR + decode) and backward (sddmm, CSR transpose, per-feature
+        # accumulations, decode against W_enc^T) of saeflow_b200.training.
+        fwd, bwd = mean(enc_ms), mean(dec_ms)
+        flops = 2.0 * T * c["d_in"] * c["d_sae"]
+        stages = {"step": "training: forward + backward", "forward_ms": round(fwd, 4), "backward_ms": round(bwd, 4),
+                  "forward_encode_tflops_incl_decode": round(flops / (fwd / 1e3) / 1e12, 2)}
+        nnz = None
+        dec_ms = []
+    elif sharded is not None:
         # Feature partition: every rank encodes all T tokens against its d_sae / world features;
         # the step (encode + CSR + decode + all-reduce of partials) is timed as a whole.
         n_feat = sharded.stop - sharded.start
@@ -510,7 +542,9 @@ def run_ours(args, rank, world, device):
         stages["encode_ms"] = round(enc, 4)
         stages["encode_tflops"] = round(achieved, 2)
     dec = mean(dec_ms)
-    if sharded is not None:
+    if args.train:
+        pass
+    elif sharded is not None:
         nnz = None
     elif cfg_id in (1, 2, 5):
         stages["csr_ms"] = round(mean(csr_ms), 4)
@@ -712,6 +746,8 @@ def main(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline time budget")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--train", action="store_true",
+                    help="one step = forward + backward of saeflow_b200.training (configs 1, 2, 4)")
     ap.add_argument("--e2e-chunk", type=int, default=8192, help="forward_host chunk size (tokens)")
     ap.add_argument("--partition", choices=["token", "feature"], default="token",
                     help="config 5: token-sharded (weights replicated) or feature-sharded (d_sae split)")

@@ -244,18 +244,23 @@ SF_API int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_v
  * dpre against W_enc^T.
  */
 
+/* out[j, i] = in[i, j], converted to out's dtype (W_enc^T for dx; dW_enc from dW_enc^T). */
+SF_API int sf_transpose(const sf_matrix *in, const sf_matrix *out, sf_stream stream);
+
 /* Bytes of workspace sf_csr_transpose needs for n_cols columns. */
 SF_API int sf_csr_transpose_workspace(int64_t n_cols, size_t *bytes);
 
 /*
- * Column view of a CSR pattern: col_ptr int64 [n_cols+1], and for each column's entries
- * (rows ascending only in expectation: the order within a column is not fixed)
- * row_idx int32 [nnz] (the entry's row) and perm int64 [nnz] (its position in the CSR).
- * An index outside [0, n_cols) is skipped and sets bit 2 of the device error.
+ * Column view of a CSR pattern: col_ptr int64 [n_cols+1], and for each column's entries (in
+ * no fixed order within the column) row_idx int32 [nnz] (the entry's row) and perm int64
+ * [nnz] (its position in the CSR). col_order (optional, int32 [n_cols + 1]) receives the
+ * columns with more than 256 entries first, then the rest, and in col_order[n_cols] the number
+ * of those hot columns: sf_csc_accumulate's schedule. An index outside
+ * [0, n_cols) is skipped and sets bit 2 of the device error.
  */
 SF_API int sf_csr_transpose(const int64_t *indptr, int64_t M, const int32_t *indices, int64_t nnz, int64_t n_cols,
-                            int64_t *col_ptr, int32_t *row_idx, int64_t *perm, void *workspace,
-                            size_t workspace_bytes, sf_stream stream);
+                            int64_t *col_ptr, int32_t *row_idx, int64_t *perm, int32_t *col_order,
+                            void *workspace, size_t workspace_bytes, sf_stream stream);
 
 /*
  * Sampled dot products on a CSR pattern:
@@ -270,11 +275,12 @@ SF_API int sf_csr_sddmm(const int64_t *indptr, int64_t M, const int32_t *indices
  * Per-column gather-accumulate over the column view of sf_csr_transpose:
  *   out[j, :] = sum_{p in column j} values[perm[p]] * R[row_idx[p], :]     (fp64 accumulation)
  *   col_sums[j] = sum_{p in column j} values[perm[p]]                      (optional, may be NULL)
- * out is fp32 [n_cols, R.cols] with row pitch ld_out; R has unit column stride.
+ * out is fp32 [n_cols, R.cols] with row pitch ld_out; R has unit column stride. col_order
+ * (optional) is the processing order from sf_csr_transpose.
  */
-SF_API int sf_csc_accumulate(const int64_t *col_ptr, int64_t n_cols, const int32_t *row_idx, const int64_t *perm,
-                             const void *values, int values_dtype, const sf_matrix *R, float *out, int64_t ld_out,
-                             float *col_sums, sf_stream stream);
+SF_API int sf_csc_accumulate(const int64_t *col_ptr, int64_t n_cols, const int32_t *col_order, int64_t nnz,
+                             const int32_t *row_idx, const int64_t *perm, const void *values, int values_dtype,
+                             const sf_matrix *R, float *out, int64_t ld_out, float *col_sums, sf_stream stream);
 
 #ifdef __cplusplus
 }

@@ -24,7 +24,7 @@ from dataclasses import dataclass
 import torch
 
 from .kernels import sparse_decode
-from .kernels.backward import csc_accumulate, csr_sddmm, csr_transpose
+from .kernels.backward import csc_accumulate, csr_sddmm, csr_transpose, transpose
 
 
 @dataclass
@@ -66,10 +66,10 @@ class _SparseForward(torch.autograd.Function):
         if need_we or need_be:
             xs = (x.float() - b_dec.float()).to(W_enc.dtype)
             dW_enc_t, db_enc = csc_accumulate(*col, dpre, xs, col_sums=True)
-            dW_enc = dW_enc_t.t().to(W_enc.dtype) if need_we else None
+            dW_enc = transpose(dW_enc_t, W_enc.dtype) if need_we else None
             db_enc = db_enc.to(W_enc.dtype) if need_be else None
         if need_x or need_bd:
-            dx = sparse_decode(indptr, indices, dpre, W_enc.t().contiguous(), None, out_dtype=torch.float32)
+            dx = sparse_decode(indptr, indices, dpre, transpose(W_enc), None, out_dtype=torch.float32)
             if need_bd:
                 db_dec = (g.float().sum(0) - dx.sum(0)).to(b_dec.dtype)
             dx = dx.to(x.dtype) if need_x else None

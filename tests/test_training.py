@@ -13,7 +13,7 @@ import torch
 import oracle
 from saeflow_b200 import training
 from saeflow_b200.kernels import csr_to_dense, device_error
-from saeflow_b200.kernels.backward import csc_accumulate, csr_sddmm, csr_transpose
+from saeflow_b200.kernels.backward import csc_accumulate, csr_sddmm, csr_transpose, transpose
 
 pytestmark = pytest.mark.gpu
 
@@ -80,12 +80,18 @@ def test_transpose_sddmm_accumulate_against_torch():
     M, n_cols, D = 200, 700, 96
     dense = (torch.rand(M, n_cols, generator=g, device="cuda") < 0.03).float() * torch.randn(
         M, n_cols, generator=g, device="cuda")
-    dense[5] = 0
-    dense[:, 13] = 0
+    dense[:, 40] = torch.randn(M, generator=g, device="cuda")  # two columns above the hot threshold (256)
+    dense[:, 41] = torch.randn(M, generator=g, device="cuda")
+    dense = torch.cat([dense, dense]).contiguous()
+    M = dense.shape[0]
+    dense[5] = 0     # an empty row
+    dense[:, 13] = 0  # an empty column
     csr = dense.to_sparse_csr()
     ip, ix, vs = csr.crow_indices(), csr.col_indices().to(torch.int32), csr.values()
-    col_ptr, row_idx, perm = csr_transpose(ip, ix, n_cols)
+    col_ptr, row_idx, perm, order = csr_transpose(ip, ix, n_cols)
     assert torch.equal(col_ptr[1:] - col_ptr[:-1], (dense != 0).sum(0))
+    assert torch.equal(order[:n_cols].long().sort().values, torch.arange(n_cols, device="cuda"))  # a permutation
+    assert sorted(order[:2].tolist()) == [40, 41] and int(order[n_cols]) == 2                   # hot ones first
     rows = torch.repeat_interleave(torch.arange(M, device="cuda"), ip[1:] - ip[:-1])
     assert torch.equal(row_idx.long(), rows[perm])        # each slot names its entry's row
     assert torch.equal(ix.long()[perm].sort().values, ix.long().sort().values)
@@ -96,7 +102,19 @@ def test_transpose_sddmm_accumulate_against_torch():
     dots = csr_sddmm(ip, ix, vs, G, W)
     want = (G[rows] * W[ix.long()]).sum(1)
     torch.testing.assert_close(dots, want, atol=1e-4, rtol=1e-4)
-    acc, sums = csc_accumulate(col_ptr, row_idx, perm, vs, G, col_sums=True)
+    acc, sums = csc_accumulate(col_ptr, row_idx, perm, order, vs, G, col_sums=True)
     torch.testing.assert_close(acc, dense.T @ G, atol=1e-4, rtol=1e-4)
     torch.testing.assert_close(sums, dense.sum(0), atol=1e-5, rtol=1e-5)
     assert device_error() == 0
+
+
+@pytest.mark.parametrize("src,dst", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float16, torch.float32)])
+@pytest.mark.parametrize("shape", [(1, 1), (33, 70), (300, 4099)])
+def test_transpose_kernel(src, dst, shape):
+    x = torch.randn(*shape, device="cuda").to(src)
+    got = transpose(x, dst)
+    assert got.shape == (shape[1], shape[0]) and got.dtype == dst and got.is_contiguous()
+    assert torch.equal(got, x.t().to(dst))
+    strided = torch.randn(shape[0], shape[1] + 5, device="cuda").to(src)[:, 2:2 + shape[1]]
+    assert torch.equal(transpose(strided, dst), strided.t().to(dst))
