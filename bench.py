@@ -332,7 +332,9 @@ def run_ours(args, rank, world, device):
             for name in ("W_enc", "b_enc", "W_dec", "b_dec"):
                 getattr(sae, name).grad = None
             return out
-        launches_per_step = 12  # forward 5 (4 for TopK) + sddmm, count, scan, scatter, 2 accumulates, decode
+        # forward 5 (4 for TopK); backward: count, scan, scatter, 2 in-column sorts, 2 x (gather, carry),
+        # 2 transposes, decode
+        launches_per_step = 17
     elif sharded is not None:
         n_chunks = (T + args.chunk_tokens - 1) // args.chunk_tokens
 

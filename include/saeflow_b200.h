@@ -239,27 +239,27 @@ SF_API int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_v
  * Backward of the sparse forward (training on sparse features). The reference has no
  * backward kernels; these implement its roadmap item (README.md:244). With the forward
  * f = act((x - b_dec) @ W_enc + b_enc) as CSR and x_hat = f @ W_dec + b_dec, and
- * g = dL/dx_hat: dpre = sf_csr_sddmm(g, W_dec) on the CSR pattern, dW_dec and dW_enc^T /
- * db_enc from sf_csc_accumulate over the transposed pattern, dx from sf_sparse_decode of
- * dpre against W_enc^T.
+ * g = dL/dx_hat: the column view of the CSR from sf_csr_transpose; dW_dec and dpre in one
+ * sf_csc_gather(values = f, R = g, W = W_dec); dW_enc^T and db_enc from
+ * sf_csc_gather(values = dpre, R = x - b_dec); dx from sf_sparse_decode of dpre against
+ * W_enc^T. sf_csr_sddmm computes dpre alone on the CSR pattern.
  */
 
 /* out[j, i] = in[i, j], converted to out's dtype (W_enc^T for dx; dW_enc from dW_enc^T). */
 SF_API int sf_transpose(const sf_matrix *in, const sf_matrix *out, sf_stream stream);
 
-/* Bytes of workspace sf_csr_transpose needs for n_cols columns. */
-SF_API int sf_csr_transpose_workspace(int64_t n_cols, size_t *bytes);
+/* Bytes of workspace sf_csr_transpose needs for n_cols columns and nnz entries. */
+SF_API int sf_csr_transpose_workspace(int64_t n_cols, int64_t nnz, size_t *bytes);
 
 /*
- * Column view of a CSR pattern: col_ptr int64 [n_cols+1], and for each column's entries (in
- * no fixed order within the column) row_idx int32 [nnz] (the entry's row) and perm int64
- * [nnz] (its position in the CSR). col_order (optional, int32 [n_cols + 1]) receives the
- * columns with more than 256 entries first, then the rest, and in col_order[n_cols] the number
- * of those hot columns: sf_csc_accumulate's schedule. An index outside
- * [0, n_cols) is skipped and sets bit 2 of the device error.
+ * Column view of a CSR pattern (the CSR of its transpose): col_ptr int64 [n_cols+1], and for
+ * each column's entries, rows ascending, row_idx int32 [nnz] (the entry's row), perm int64 [nnz]
+ * (its position in the CSR) and col_idx int32 [nnz] (its column; optional, may be NULL; required
+ * by sf_csc_gather). An index outside [0, n_cols) is skipped and sets bit 2 of the device error;
+ * a (row, column) pair present twice sets bit 4.
  */
 SF_API int sf_csr_transpose(const int64_t *indptr, int64_t M, const int32_t *indices, int64_t nnz, int64_t n_cols,
-                            int64_t *col_ptr, int32_t *row_idx, int64_t *perm, int32_t *col_order,
+                            int64_t *col_ptr, int32_t *row_idx, int64_t *perm, int32_t *col_idx,
                             void *workspace, size_t workspace_bytes, sf_stream stream);
 
 /*
@@ -271,16 +271,24 @@ SF_API int sf_csr_transpose(const int64_t *indptr, int64_t M, const int32_t *ind
 SF_API int sf_csr_sddmm(const int64_t *indptr, int64_t M, const int32_t *indices, const sf_matrix *G,
                         const sf_matrix *W, const void *values, int values_dtype, float *out, sf_stream stream);
 
+/* Bytes of workspace sf_csc_gather needs for nnz entries gathering rows of R (0 when it needs none). */
+SF_API int sf_csc_gather_workspace(int64_t nnz, const sf_matrix *R, size_t *bytes);
+
 /*
- * Per-column gather-accumulate over the column view of sf_csr_transpose:
- *   out[j, :] = sum_{p in column j} values[perm[p]] * R[row_idx[p], :]     (fp64 accumulation)
- *   col_sums[j] = sum_{p in column j} values[perm[p]]                      (optional, may be NULL)
- * out is fp32 [n_cols, R.cols] with row pitch ld_out; R has unit column stride. col_order
- * (optional) is the processing order from sf_csr_transpose.
+ * Per-column gather over the column view of sf_csr_transpose (p runs over column j's entries
+ * in the view's order, rows ascending):
+ *   out[j, :]     = sum_p values[perm[p]] * R[row_idx[p], :]            (fp32 sums, out's dtype)
+ *   col_sums[j]   = sum_p values[perm[p]]                                (optional, may be NULL)
+ *   dots[perm[p]] = (values[perm[p]] != 0) * R[row_idx[p], :] . W[j, :]  (optional: W NULL or
+ *                                                                         W->data NULL skips it)
+ * R [M, D] and W [n_cols, D] of one dtype with unit column stride; out [n_cols, D] in any
+ * dtype; values in values_dtype, indexed by CSR position. Rows whose byte width and pitch are
+ * multiples of 16 go through the shared-memory bulk-copy kernel, others through a plain one.
  */
-SF_API int sf_csc_accumulate(const int64_t *col_ptr, int64_t n_cols, const int32_t *col_order, int64_t nnz,
-                             const int32_t *row_idx, const int64_t *perm, const void *values, int values_dtype,
-                             const sf_matrix *R, float *out, int64_t ld_out, float *col_sums, sf_stream stream);
+SF_API int sf_csc_gather(const int64_t *col_ptr, int64_t n_cols, const int32_t *col_idx, int64_t nnz,
+                         const int32_t *row_idx, const int64_t *perm, const void *values, int values_dtype,
+                         const sf_matrix *R, const sf_matrix *W, float *dots, const sf_matrix *out,
+                         float *col_sums, void *workspace, size_t workspace_bytes, sf_stream stream);
 
 #ifdef __cplusplus
 }

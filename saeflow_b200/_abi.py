@@ -63,12 +63,13 @@ SIGNATURES = {
     "sf_dense_to_csr": (_c.c_int, [_MP, _P, _P, _P, _c.c_int, _P]),
     "sf_sparse_decode": (_c.c_int, [_P, _c.c_int64, _P, _P, _c.c_int, _MP, _VP, _MP, _P]),
     "sf_transpose": (_c.c_int, [_MP, _MP, _P]),
-    "sf_csr_transpose_workspace": (_c.c_int, [_c.c_int64, _SIZE_P]),
+    "sf_csr_transpose_workspace": (_c.c_int, [_c.c_int64, _c.c_int64, _SIZE_P]),
     "sf_csr_transpose": (_c.c_int, [_P, _c.c_int64, _P, _c.c_int64, _c.c_int64, _P, _P, _P, _P, _P, _c.c_size_t,
                                     _P]),
     "sf_csr_sddmm": (_c.c_int, [_P, _c.c_int64, _P, _MP, _MP, _P, _c.c_int, _P, _P]),
-    "sf_csc_accumulate": (_c.c_int, [_P, _c.c_int64, _P, _c.c_int64, _P, _P, _P, _c.c_int, _MP, _P, _c.c_int64, _P,
-                                     _P]),
+    "sf_csc_gather_workspace": (_c.c_int, [_c.c_int64, _MP, _SIZE_P]),
+    "sf_csc_gather": (_c.c_int, [_P, _c.c_int64, _P, _c.c_int64, _P, _P, _P, _c.c_int, _MP, _MP, _P, _MP, _P, _P,
+                                 _c.c_size_t, _P]),
     "sf_topk_encode_workspace": (_c.c_int, [_MP, _MP, _c.c_int, _c.c_int, _SIZE_P]),
     "sf_topk_encode": (_c.c_int, [_MP, _MP, _VP, _VP, _c.c_int, _P, _P, _c.c_int, _c.c_int, _P,
                                   _c.c_size_t, _P]),

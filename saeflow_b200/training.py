@@ -9,10 +9,13 @@ JumpReLU threshold receives no gradient here: the step function has zero derivat
 everywhere, and a straight-through estimator for it is a training choice left to the
 caller.
 
-Backward, with g = dL/dx_hat and the forward's CSR (indptr, indices, values):
-    dpre     = g[row] . W_dec[col] on the CSR pattern            csr_sddmm
-    dW_dec   = per feature, sum of value * g[row]                  csc_accumulate
+Backward, with g = dL/dx_hat and the forward's CSR (indptr, indices, values), over the
+column view of the CSR (csr_transpose, rows ascending within each column, so every sum is
+taken in one fixed order and the gradients are the same from run to run):
+    dW_dec   = per feature, sum of value * g[row]           } one csc_gather pass over the
+    dpre     = g[row] . W_dec[col] at each active entry     } gathered rows of g
     dW_enc^T = per feature, sum of dpre * (x - b_dec)[row], db_enc = per feature sum of dpre
+                                                              (a second csc_gather pass)
     dx       = dpre @ W_enc^T (the CSR decode against W_enc^T), db_dec = sum_rows (g - dx)
 (x - b_dec) is taken rounded to W_enc's dtype, the operand the encoder multiplied.
 """
@@ -24,7 +27,7 @@ from dataclasses import dataclass
 import torch
 
 from .kernels import sparse_decode
-from .kernels.backward import csc_accumulate, csr_sddmm, csr_transpose, transpose
+from .kernels.backward import csc_gather, csr_sddmm, csr_transpose, transpose
 
 
 @dataclass
@@ -55,18 +58,23 @@ class _SparseForward(torch.autograd.Function):
         x, W_enc, W_dec, b_dec, indptr, indices, values = ctx.saved_tensors
         need_x, need_we, need_be, need_wd, need_bd = ctx.needs_input_grad[:5]
         g = g.contiguous()
+        if g.dtype != W_dec.dtype:
+            g = g.to(W_dec.dtype)
         d_sae = W_enc.shape[1]
         dx = dW_enc = db_enc = dW_dec = db_dec = None
-        dpre = csr_sddmm(indptr, indices, values, g.to(W_dec.dtype), W_dec)
-        col = None
-        if need_wd or need_we or need_be:
-            col = csr_transpose(indptr, indices, d_sae)
-        if need_wd:
-            dW_dec = csc_accumulate(*col, values, g).to(W_dec.dtype)
+        need_dpre = need_x or need_bd or need_we or need_be
+        col = csr_transpose(indptr, indices, d_sae) if (need_wd or need_we or need_be) else None
+        dpre = None
+        if need_wd and need_dpre:
+            dW_dec, dpre = csc_gather(*col, values, g, W=W_dec, out_dtype=W_dec.dtype)
+        elif need_wd:
+            dW_dec = csc_gather(*col, values, g, out_dtype=W_dec.dtype)
+        elif need_dpre:
+            dpre = csr_sddmm(indptr, indices, values, g, W_dec)
         if need_we or need_be:
             xs = (x.float() - b_dec.float()).to(W_enc.dtype)
-            dW_enc_t, db_enc = csc_accumulate(*col, dpre, xs, col_sums=True)
-            dW_enc = transpose(dW_enc_t, W_enc.dtype) if need_we else None
+            dW_enc_t, db_enc = csc_gather(*col, dpre, xs, out_dtype=W_enc.dtype, col_sums=True)
+            dW_enc = transpose(dW_enc_t) if need_we else None
             db_enc = db_enc.to(W_enc.dtype) if need_be else None
         if need_x or need_bd:
             dx = sparse_decode(indptr, indices, dpre, transpose(W_enc), None, out_dtype=torch.float32)

@@ -13,7 +13,7 @@ import torch
 import oracle
 from saeflow_b200 import training
 from saeflow_b200.kernels import csr_to_dense, device_error
-from saeflow_b200.kernels.backward import csc_accumulate, csr_sddmm, csr_transpose, transpose
+from saeflow_b200.kernels.backward import csc_gather, csr_sddmm, csr_transpose, transpose
 
 pytestmark = pytest.mark.gpu
 
@@ -74,37 +74,120 @@ def test_backward_matches_autograd_on_the_active_set(activation, dtype, shape):
     assert device_error() == 0
 
 
-def test_transpose_sddmm_accumulate_against_torch():
-    """The three kernels on a random CSR pattern (with empty rows and empty columns)."""
-    g = torch.Generator(device="cuda").manual_seed(3)
-    M, n_cols, D = 200, 700, 96
-    dense = (torch.rand(M, n_cols, generator=g, device="cuda") < 0.03).float() * torch.randn(
+def _random_csr(M, n_cols, density, full_cols=(), seed=3):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dense = (torch.rand(M, n_cols, generator=g, device="cuda") < density).float() * torch.randn(
         M, n_cols, generator=g, device="cuda")
-    dense[:, 40] = torch.randn(M, generator=g, device="cuda")  # two columns above the hot threshold (256)
-    dense[:, 41] = torch.randn(M, generator=g, device="cuda")
-    dense = torch.cat([dense, dense]).contiguous()
-    M = dense.shape[0]
-    dense[5] = 0     # an empty row
-    dense[:, 13] = 0  # an empty column
+    for j in full_cols:  # columns with an entry in every row: they span several ranges
+        dense[:, j] = torch.randn(M, generator=g, device="cuda")
+    if M > 5:
+        dense[5] = 0      # an empty row
+    if n_cols > 13:
+        dense[:, 13] = 0  # an empty column
+    dense[:, :2] = 0      # empty columns before the first entry
+    dense[:, -3:] = 0     # ... and after the last
     csr = dense.to_sparse_csr()
-    ip, ix, vs = csr.crow_indices(), csr.col_indices().to(torch.int32), csr.values()
-    col_ptr, row_idx, perm, order = csr_transpose(ip, ix, n_cols)
-    assert torch.equal(col_ptr[1:] - col_ptr[:-1], (dense != 0).sum(0))
-    assert torch.equal(order[:n_cols].long().sort().values, torch.arange(n_cols, device="cuda"))  # a permutation
-    assert sorted(order[:2].tolist()) == [40, 41] and int(order[n_cols]) == 2                   # hot ones first
+    return dense, csr.crow_indices(), csr.col_indices().to(torch.int32), csr.values()
+
+
+def test_csr_transpose_is_the_column_view():
+    """The column view is the CSR of the transpose: rows ascend within each column."""
+    dense, ip, ix, vs = _random_csr(400, 700, 0.03, full_cols=(40, 41))
+    M, n_cols = dense.shape
+    col_ptr, row_idx, perm, col_idx = csr_transpose(ip, ix, n_cols)
+    csc = dense.to_sparse_csc()
+    assert torch.equal(col_ptr, csc.ccol_indices())
+    assert torch.equal(row_idx.long(), csc.row_indices())
+    assert torch.equal(vs[perm], csc.values())
     rows = torch.repeat_interleave(torch.arange(M, device="cuda"), ip[1:] - ip[:-1])
-    assert torch.equal(row_idx.long(), rows[perm])        # each slot names its entry's row
-    assert torch.equal(ix.long()[perm].sort().values, ix.long().sort().values)
+    assert torch.equal(row_idx.long(), rows[perm])
     cols = torch.repeat_interleave(torch.arange(n_cols, device="cuda"), col_ptr[1:] - col_ptr[:-1])
-    assert torch.equal(ix.long()[perm], cols)             # ... and sits in its own column
-    G = torch.randn(M, D, generator=g, device="cuda")
-    W = torch.randn(n_cols, D, generator=g, device="cuda")
-    dots = csr_sddmm(ip, ix, vs, G, W)
-    want = (G[rows] * W[ix.long()]).sum(1)
-    torch.testing.assert_close(dots, want, atol=1e-4, rtol=1e-4)
-    acc, sums = csc_accumulate(col_ptr, row_idx, perm, order, vs, G, col_sums=True)
-    torch.testing.assert_close(acc, dense.T @ G, atol=1e-4, rtol=1e-4)
-    torch.testing.assert_close(sums, dense.sum(0), atol=1e-5, rtol=1e-5)
+    assert torch.equal(col_idx.long(), cols)
+    assert torch.equal(ix.long()[perm], cols)
+    assert device_error() == 0
+
+
+def test_csr_transpose_long_column_across_bitmap_windows():
+    """A column with entries in 600000 rows: the in-column sort works in windows of rows."""
+    M = 600_000
+    r = torch.arange(M, device="cuda")
+    second = 10 + (r * 7919) % 1000          # a second entry per row, in a shuffled column
+    idx = torch.stack([torch.full_like(r, 5), second], 1).sort(1).values.reshape(-1).to(torch.int32)
+    ip = torch.arange(0, 2 * M + 1, 2, device="cuda")
+    col_ptr, row_idx, perm, col_idx = csr_transpose(ip, idx, 1010)
+    assert int(col_ptr[6] - col_ptr[5]) == M
+    assert torch.equal(row_idx[col_ptr[5]:col_ptr[6]].long(), r)
+    rows = torch.repeat_interleave(torch.arange(M, device="cuda"), 2)
+    assert torch.equal(row_idx.long(), rows[perm])
+    for j in (10, 500, 1009):
+        seg = row_idx[col_ptr[j]:col_ptr[j + 1]].long()
+        assert torch.equal(seg, r[second == j])
+    assert device_error() == 0
+
+
+@pytest.mark.parametrize("case", [
+    # (M, n_cols, D, density, full columns, R dtype, out dtype)
+    (400, 700, 96, 0.03, (40, 41), torch.float32, torch.float32),   # columns across ranges
+    (800, 3000, 128, 0.01, (7, 2000), torch.bfloat16, torch.bfloat16),
+    (300, 500, 64, 0.05, (), torch.float16, torch.float32),
+    (50, 90, 40, 0.02, (), torch.bfloat16, torch.float32),            # few entries: one range
+    (200, 300, 37, 0.05, (3,), torch.float32, torch.bfloat16),        # unaligned rows: plain kernel
+    (64, 200, 4104, 0.05, (9,), torch.float32, torch.float32),        # two D-pieces, dots apart
+    (300, 400, 2304, 0.05, (1, 2), torch.bfloat16, torch.bfloat16),   # the benchmark's row width
+])
+def test_csc_gather_against_torch(case):
+    M, n_cols, D, density, full, rdt, odt = case
+    dense, ip, ix, vs = _random_csr(M, n_cols, density, full_cols=full)
+    vs = vs.to(rdt)
+    vs[::7] = 0  # entries whose value is zero get no dot product
+    dense = csr_to_dense(ip, ix, vs.float(), n_cols)
+    col = csr_transpose(ip, ix, n_cols)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    R = torch.randn(M, D, generator=g, device="cuda").to(rdt)
+    W = torch.randn(n_cols, D, generator=g, device="cuda").to(rdt)
+    out, sums, dots = csc_gather(*col, vs, R, W=W, out_dtype=odt, col_sums=True)
+    assert out.dtype == odt and out.shape == (n_cols, D)
+    want = (dense.double().T @ R.double()).float()
+    tol = 2e-5 if odt == torch.float32 else 8e-3
+    torch.testing.assert_close(out.float(), want.to(odt).float(), atol=tol * (1 + M ** 0.5), rtol=tol)
+    torch.testing.assert_close(sums, dense.double().sum(0).float(), atol=1e-5, rtol=1e-5)
+    rows = torch.repeat_interleave(torch.arange(M, device="cuda"), ip[1:] - ip[:-1])
+    want_dots = (R.float()[rows] * W.float()[ix.long()]).sum(1) * (vs.float() != 0)
+    torch.testing.assert_close(dots, want_dots, atol=2e-4 * D ** 0.5, rtol=1e-4)
+    torch.testing.assert_close(dots, csr_sddmm(ip, ix, vs, R, W), atol=2e-4 * D ** 0.5, rtol=1e-4)
+    # the sums are taken in the column view's fixed order: the same bits every call, with or
+    # without the dot products and column sums
+    assert torch.equal(csc_gather(*col, vs, R, out_dtype=odt), out)
+    out2, _, dots2 = csc_gather(*col, vs, R, W=W, out_dtype=odt, col_sums=True)
+    assert torch.equal(out2, out) and torch.equal(dots2, dots)
+    assert device_error() == 0
+
+
+def test_csc_gather_without_entries():
+    M, n_cols, D = 10, 20, 32
+    ip = torch.zeros(M + 1, dtype=torch.int64, device="cuda")
+    ix = torch.zeros(0, dtype=torch.int32, device="cuda")
+    vs = torch.zeros(0, dtype=torch.float32, device="cuda")
+    col = csr_transpose(ip, ix, n_cols)
+    out, sums = csc_gather(*col, vs, torch.randn(M, D, device="cuda"), out_dtype=torch.bfloat16, col_sums=True)
+    assert torch.equal(out, torch.zeros(n_cols, D, dtype=torch.bfloat16, device="cuda"))
+    assert torch.equal(sums, torch.zeros(n_cols, device="cuda"))
+    assert device_error() == 0
+
+
+def test_backward_is_deterministic():
+    """Two backward passes on the same inputs give the same gradient bits."""
+    sae = _sae(256, 2048, "jumprelu", torch.bfloat16)
+    x = (torch.randn(1000, 256, device="cuda") * 1.5).to(torch.bfloat16)
+    r = torch.randn(1000, 256, device="cuda").to(torch.bfloat16)
+    grads = []
+    for _ in range(2):
+        for name in ("W_enc", "b_enc", "W_dec", "b_dec"):
+            getattr(sae, name).grad = None
+        training.forward(sae, x).backward(r)
+        grads.append([getattr(sae, n).grad.clone() for n in ("W_enc", "b_enc", "W_dec", "b_dec")])
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
     assert device_error() == 0
 
 
