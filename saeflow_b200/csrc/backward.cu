@@ -300,7 +300,8 @@ __device__ __forceinline__ bool mbar_wait_suspend(uint64_t *bar, uint32_t parity
 // range order. A column without entries is written as zeros by the range in which its (empty)
 // entry span starts.
 constexpr int kGatherMaxPieceBytes = 16384;
-constexpr int kGatherRingBytes = 96 * 1024;  // two CTAs per SM
+constexpr int kGatherCtasPerSm = 2;
+constexpr int kGatherRingBytes = 192 * 1024 / kGatherCtasPerSm;
 constexpr int kGatherStages = 4;
 constexpr int kGatherMaxWarps = 16;    // consumer warps
 constexpr int kGatherMinEntries = 64;  // entries per range at least
@@ -378,6 +379,13 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
     const bool head = a > 0 && col_at(a - 1) == first_col;
     const bool tail = b < g.nnz && col_at(b) == last_col;
 
+    if (piece_bytes < g.slot_stride) {  // zero the slot padding (the copies never write it)
+        const uint32_t pad = g.slot_stride - piece_bytes;
+        for (uint32_t i = threadIdx.x * 4; i < (uint32_t)S * pad; i += blockDim.x * 4) {
+            const uint32_t sl = i / pad, o = i - sl * pad;
+            *reinterpret_cast<uint32_t *>(ring + (size_t)sl * g.slot_stride + piece_bytes + o) = 0u;
+        }
+    }
     if (threadIdx.x == 0) {
         for (int st = 0; st < NS; ++st) {
             mbar_init(&full[st], G);
@@ -557,12 +565,13 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
     const int ct = threadIdx.x - 32;
     const int nct = g.consumer_warps * 32;
     float acc[CPT][EPV];
-    float wv[CPT][EPV];
+    float wv[DOT ? CPT : 1][DOT ? EPV : 1];
     double vsum = 0.0;
     int32_t cur = -1;
     char *out = reinterpret_cast<char *>(g.out);
     const size_t oes = g.out_dtype == SF_F32 ? 4 : 2;
-    const bool write_sums = g.col_sums != nullptr && q == 0;
+    const bool sums = g.col_sums != nullptr;  // the carry holds them for the range's end columns
+    const bool write_sums = sums && q == 0;
     const bool vec = g.out_vec != 0;
 
     auto zero_cols = [&](int64_t lo, int64_t hi) {  // columns [lo, hi) have no entries
@@ -608,50 +617,29 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
         zero_cols((int64_t)col_at(a - 1) + 1, first_col);
     }
     // A stage's rows have all landed once its full barrier completes, so the loop loads the
-    // next slot's metadata and chunks before working on the current one.
-    auto slot_meta = [&](int s) { return *reinterpret_cast<const int4 *>(&meta[s]); };  // v, col, kind, row
-    auto slot_data = [&](int s, uint4 (&u)[CPT]) {
+    // next slot's metadata and chunks before working on the current one, alternating between
+    // two register sets.
+    auto load = [&](int s, int4 &m, uint4 (&u)[CPT]) {
+        m = *reinterpret_cast<const int4 *>(&meta[s]);  // v, col, kind, row
         const uint4 *src = reinterpret_cast<const uint4 *>(ring + (size_t)s * g.slot_stride);
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) {
-            const int ch = ct + k * nct;
-            u[k] = ch < n_chunks ? src[ch] : make_uint4(0u, 0u, 0u, 0u);
-        }
+        for (int k = 0; k < CPT; ++k) u[k] = src[ct + k * nct];
     };
-    bool end = false;
-    for (int st = 0, phase = 0; !end; ++st) {
-        if (st == NS) st = 0, phase ^= 1;
-        if (!mbar_wait_suspend(&full[st], (uint32_t)phase, abort_flag, g.err)) return;
-        int4 mn = slot_meta(st * G);
-        uint4 un[CPT];
-        slot_data(st * G, un);
-        for (int i = 0; i < G; ++i) {
-            const int s = st * G + i;
-            const int4 m = mn;
-            uint4 u[CPT];
-#pragma unroll
-            for (int k = 0; k < CPT; ++k) u[k] = un[k];
-            if (m.z == 2) {
-                end = true;
-                break;
+    auto work = [&](int s, const int4 &m, const uint4 (&u)[CPT]) {
+        const int32_t mcol = m.y;
+        if (mcol != cur) {
+            if (cur >= 0) {
+                flush(cur);
+                zero_cols((int64_t)cur + 1, mcol);
             }
-            if (i + 1 < G) {
-                mn = slot_meta(s + 1);
-                slot_data(s + 1, un);
-            }
-            const int32_t mcol = m.y;
-            if (mcol != cur) {
-                if (cur >= 0) {
-                    flush(cur);
-                    zero_cols((int64_t)cur + 1, mcol);
-                }
-                cur = mcol;
+            cur = mcol;
 #pragma unroll
-                for (int k = 0; k < CPT; ++k)
+            for (int k = 0; k < CPT; ++k)
 #pragma unroll
-                    for (int e = 0; e < EPV; ++e) acc[k][e] = 0.f;
-                vsum = 0.0;
-            }
+                for (int e = 0; e < EPV; ++e) acc[k][e] = 0.f;
+            vsum = 0.0;
+        }
+        if constexpr (DOT) {  // only the dot products put rows of W in the stream
             if (m.z == 1) {
 #pragma unroll
                 for (int k = 0; k < CPT; ++k) {
@@ -659,26 +647,50 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
 #pragma unroll
                     for (int e = 0; e < EPV; ++e) wv[k][e] = to_f32(el[e]);
                 }
-            } else {
-                const float vf = __int_as_float(m.x);
-                float dp = 0.f;
-#pragma unroll
-                for (int k = 0; k < CPT; ++k) {
-                    const RT *el = reinterpret_cast<const RT *>(&u[k]);
-#pragma unroll
-                    for (int e = 0; e < EPV; ++e) {
-                        const float x = to_f32(el[e]);
-                        acc[k][e] = fmaf(vf, x, acc[k][e]);
-                        if constexpr (DOT) dp = fmaf(x, wv[k][e], dp);
-                    }
-                }
-                vsum += (double)vf;
-                if constexpr (DOT) {
-#pragma unroll
-                    for (int off = 16; off > 0; off >>= 1) dp += __shfl_xor_sync(0xffffffffu, dp, off);
-                    if (lane == 0) dotp[s * kGatherMaxWarps + cw] = dp;
-                }
+                return;
             }
+        }
+        const float vf = __int_as_float(m.x);
+        float dp = 0.f;
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) {
+            const RT *el = reinterpret_cast<const RT *>(&u[k]);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) {
+                const float x = to_f32(el[e]);
+                acc[k][e] = fmaf(vf, x, acc[k][e]);
+                if constexpr (DOT) dp = fmaf(x, wv[k][e], dp);
+            }
+        }
+        if (sums) vsum += (double)vf;
+        if constexpr (DOT) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) dp += __shfl_xor_sync(0xffffffffu, dp, off);
+            if (lane == 0) dotp[s * kGatherMaxWarps + cw] = dp;
+        }
+    };
+    bool end = false;
+    for (int st = 0, phase = 0; !end; ++st) {
+        if (st == NS) st = 0, phase ^= 1;
+        if (!mbar_wait_suspend(&full[st], (uint32_t)phase, abort_flag, g.err)) return;
+        const int s0 = st * G;
+        int4 ma, mb;
+        uint4 ua[CPT], ub[CPT];
+        load(s0, ma, ua);
+        for (int i = 0; i < G; i += 2) {
+            if (ma.z == 2) {
+                end = true;
+                break;
+            }
+            if (i + 1 < G) load(s0 + i + 1, mb, ub);
+            work(s0 + i, ma, ua);
+            if (i + 1 >= G) break;
+            if (mb.z == 2) {
+                end = true;
+                break;
+            }
+            if (i + 2 < G) load(s0 + i + 2, ma, ua);
+            work(s0 + i + 1, mb, ub);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
@@ -921,14 +933,17 @@ GatherPlan plan_gather(int64_t nnz, int64_t D, size_t es, bool aligned, bool dot
     }
     while ((chunks + 32 * p.cpt - 1) / (32 * p.cpt) > gather_max_warps(p.cpt)) ++p.cpt;
     p.consumer_warps = (int)((chunks + 32 * p.cpt - 1) / (32 * p.cpt));
-    p.slot_stride = (uint32_t)((p.piece_elems * (int64_t)es + 127) / 128 * 128);
+    // A slot spans every consumer thread's chunks; the bytes past the row piece stay zero, so
+    // the consumers read their chunks unconditionally.
+    p.slot_stride = (uint32_t)((std::max<int64_t>(p.piece_elems * (int64_t)es, (int64_t)p.consumer_warps * 32 * p.cpt * 16) + 127) /
+                               128 * 128);
     int slots = 2;
     while (slots < 64 && gather_header_bytes(slots + 1) + (size_t)(slots + 1) * p.slot_stride <= kGatherRingBytes)
         ++slots;
     p.group = std::min(32, std::max(1, slots / kGatherStages));
     p.slots = slots / p.group * p.group;
     p.smem = gather_header_bytes(p.slots) + (size_t)p.slots * p.slot_stride;
-    const int64_t max_ranges = 2 * (int64_t)num_sms();
+    const int64_t max_ranges = kGatherCtasPerSm * (int64_t)num_sms();
     int64_t ranges = std::min<int64_t>(max_ranges, (nnz + kGatherMinEntries - 1) / kGatherMinEntries);
     ranges = std::max<int64_t>(ranges, 1);
     p.per_range = (nnz + ranges - 1) / ranges;
