@@ -892,6 +892,59 @@ __global__ void __launch_bounds__(256) transpose_kernel(const IT *__restrict__ i
     }
 }
 
+// The same on 64 x 64 tiles with two elements per thread along the contiguous dimension, for
+// even extents and pitches: each warp reads and writes 64 consecutive elements (128 bytes of a
+// 16-bit matrix) per row instead of 32.
+template <typename T>
+struct Pair;
+template <>
+struct Pair<float> {
+    using V = float2;
+    static __device__ __forceinline__ void get(const V &v, float &a, float &b) { a = v.x, b = v.y; }
+    static __device__ __forceinline__ V make(float a, float b) { return make_float2(a, b); }
+};
+template <>
+struct Pair<__nv_bfloat16> {
+    using V = __nv_bfloat162;
+    static __device__ __forceinline__ void get(const V &v, float &a, float &b) {
+        a = __low2float(v), b = __high2float(v);
+    }
+    static __device__ __forceinline__ V make(float a, float b) { return __floats2bfloat162_rn(a, b); }
+};
+template <>
+struct Pair<__half> {
+    using V = __half2;
+    static __device__ __forceinline__ void get(const V &v, float &a, float &b) {
+        a = __low2float(v), b = __high2float(v);
+    }
+    static __device__ __forceinline__ V make(float a, float b) { return __floats2half2_rn(a, b); }
+};
+
+template <typename IT, typename OT>
+__global__ void __launch_bounds__(256) transpose2_kernel(const IT *__restrict__ in, int64_t rows, int64_t cols,
+                                                         int64_t ldi, OT *__restrict__ out, int64_t ldo) {
+    __shared__ float tile[64][65];
+    const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads, 2 elements each
+#pragma unroll
+    for (int k = 0; k < 64; k += 8) {
+        const int64_t r = r0 + ty + k, c = c0 + 2 * tx;
+        float a = 0.f, b = 0.f;
+        if (r < rows && c < cols)  // cols is even, so c + 1 < cols too
+            Pair<IT>::get(*reinterpret_cast<const typename Pair<IT>::V *>(in + r * ldi + c), a, b);
+        tile[ty + k][2 * tx] = a;
+        tile[ty + k][2 * tx + 1] = b;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 64; k += 8) {
+        const int64_t orow = c0 + ty + k, oc = r0 + 2 * tx;  // out is [cols, rows]
+        if (orow < cols && oc < rows)  // rows is even
+            *reinterpret_cast<typename Pair<OT>::V *>(out + orow * ldo + oc) =
+                Pair<OT>::make(tile[2 * tx][ty + k], tile[2 * tx + 1][ty + k]);
+    }
+}
+
 template <typename F>
 int by_dtype(int dt, F &&f) {
     if (dt == SF_F32) return f(float{});
@@ -1154,11 +1207,23 @@ int sf_transpose(const sf_matrix *in, const sf_matrix *out, sf_stream stream) {
     if ((in->cols + 31) / 32 > (int64_t)INT32_MAX || (in->rows + 31) / 32 > 65535)
         return set_error(SF_ERR_UNSUPPORTED, "transpose grid too large");
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const size_t ies = dtype_size(in->dtype), oes = dtype_size(out->dtype);
+    const bool pairs = in->rows % 2 == 0 && in->cols % 2 == 0 && in->stride_row % 2 == 0 && out->stride_row % 2 == 0 &&
+                       (reinterpret_cast<uintptr_t>(in->data) % (2 * ies)) == 0 &&
+                       (reinterpret_cast<uintptr_t>(out->data) % (2 * oes)) == 0 && (in->rows + 63) / 64 <= 65535;
     dim3 grid((unsigned)((in->cols + 31) / 32), (unsigned)((in->rows + 31) / 32));
+    if (pairs) grid = dim3((unsigned)((in->cols + 63) / 64), (unsigned)((in->rows + 63) / 64));
     return by_dtype(in->dtype, [&](auto itag) {
         using IT = decltype(itag);
         return by_dtype(out->dtype, [&](auto otag) {
             using OT = decltype(otag);
+            if (pairs) {
+                transpose2_kernel<IT, OT><<<grid, 256, 0, s>>>(reinterpret_cast<const IT *>(in->data), in->rows,
+                                                               in->cols, in->stride_row,
+                                                               reinterpret_cast<OT *>(const_cast<void *>(out->data)),
+                                                               out->stride_row);
+                return check_cuda(cudaGetLastError(), "transpose launch");
+            }
             transpose_kernel<IT, OT><<<grid, 256, 0, s>>>(reinterpret_cast<const IT *>(in->data), in->rows, in->cols,
                                                           in->stride_row,
                                                           reinterpret_cast<OT *>(const_cast<void *>(out->data)),

@@ -193,11 +193,12 @@ def test_backward_is_deterministic():
 
 @pytest.mark.parametrize("src,dst", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
                                      (torch.float16, torch.float32)])
-@pytest.mark.parametrize("shape", [(1, 1), (33, 70), (300, 4099)])
+@pytest.mark.parametrize("shape", [(1, 1), (33, 70), (300, 4099), (64, 130), (130, 4098)])
 def test_transpose_kernel(src, dst, shape):
     x = torch.randn(*shape, device="cuda").to(src)
     got = transpose(x, dst)
     assert got.shape == (shape[1], shape[0]) and got.dtype == dst and got.is_contiguous()
     assert torch.equal(got, x.t().to(dst))
-    strided = torch.randn(shape[0], shape[1] + 5, device="cuda").to(src)[:, 2:2 + shape[1]]
-    assert torch.equal(transpose(strided, dst), strided.t().to(dst))
+    for extra in (5, 6):  # odd and even row pitch
+        strided = torch.randn(shape[0], shape[1] + extra, device="cuda").to(src)[:, 2:2 + shape[1]]
+        assert torch.equal(transpose(strided, dst), strided.t().to(dst))
