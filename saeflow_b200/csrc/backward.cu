@@ -625,7 +625,7 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
 #pragma unroll
         for (int k = 0; k < CPT; ++k) u[k] = src[ct + k * nct];
     };
-    auto work = [&](int s, const int4 &m, const uint4 (&u)[CPT]) {
+    auto work = [&](const int4 &m, const uint4 (&u)[CPT]) -> float {  // the lane's dot product part
         const int32_t mcol = m.y;
         if (mcol != cur) {
             if (cur >= 0) {
@@ -647,7 +647,7 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
 #pragma unroll
                     for (int e = 0; e < EPV; ++e) wv[k][e] = to_f32(el[e]);
                 }
-                return;
+                return 0.f;
             }
         }
         const float vf = __int_as_float(m.x);
@@ -663,10 +663,25 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
             }
         }
         if (sums) vsum += (double)vf;
+        return dp;
+    };
+    // Warp sums of the dot product parts of one slot, or of two at once: the first butterfly
+    // step sends each half-warp the other slot's parts, so two slots cost five shuffles.
+    auto reduce1 = [&](float d, int s) {
         if constexpr (DOT) {
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) dp += __shfl_xor_sync(0xffffffffu, dp, off);
-            if (lane == 0) dotp[s * kGatherMaxWarps + cw] = dp;
+            for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+            if (lane == 0) dotp[s * kGatherMaxWarps + cw] = d;
+        }
+    };
+    auto reduce2 = [&](float da, int sa, float db, int sb) {
+        if constexpr (DOT) {
+            const bool lo = lane < 16;
+            float d = (lo ? da : db) + __shfl_xor_sync(0xffffffffu, lo ? db : da, 16);
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+            if (lane == 0) dotp[sa * kGatherMaxWarps + cw] = d;
+            if (lane == 16) dotp[sb * kGatherMaxWarps + cw] = d;
         }
     };
     bool end = false;
@@ -683,14 +698,15 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
                 break;
             }
             if (i + 1 < G) load(s0 + i + 1, mb, ub);
-            work(s0 + i, ma, ua);
-            if (i + 1 >= G) break;
-            if (mb.z == 2) {
-                end = true;
+            const float da = work(ma, ua);
+            if (i + 1 >= G || mb.z == 2) {
+                reduce1(da, s0 + i);
+                end = i + 1 < G;
                 break;
             }
             if (i + 2 < G) load(s0 + i + 2, ma, ua);
-            work(s0 + i + 1, mb, ub);
+            const float db = work(mb, ub);
+            reduce2(da, s0 + i, db, s0 + i + 1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);

@@ -72,14 +72,17 @@ class _SparseForward(torch.autograd.Function):
         elif need_dpre:
             dpre = csr_sddmm(indptr, indices, values, g, W_dec)
         if need_we or need_be:
-            xs = (x.float() - b_dec.float()).to(W_enc.dtype)
+            if x.dtype == b_dec.dtype == W_enc.dtype:
+                xs = x - b_dec  # torch subtracts 16-bit operands in fp32 and rounds once, as below
+            else:
+                xs = (x.float() - b_dec.float()).to(W_enc.dtype)
             dW_enc_t, db_enc = csc_gather(*col, dpre, xs, out_dtype=W_enc.dtype, col_sums=True)
             dW_enc = transpose(dW_enc_t) if need_we else None
             db_enc = db_enc.to(W_enc.dtype) if need_be else None
         if need_x or need_bd:
             dx = sparse_decode(indptr, indices, dpre, transpose(W_enc), None, out_dtype=torch.float32)
             if need_bd:
-                db_dec = (g.float().sum(0) - dx.sum(0)).to(b_dec.dtype)
+                db_dec = (g.sum(0, dtype=torch.float32) - dx.sum(0)).to(b_dec.dtype)
             dx = dx.to(x.dtype) if need_x else None
         return dx, dW_enc, db_enc, dW_dec, db_dec, None, None, None
 
