@@ -20,6 +20,7 @@
 // gathered row, so the bytes in flight are bounded by shared memory rather than registers.
 #include <algorithm>
 #include <climits>
+#include <type_traits>
 
 #include "sf_common.cuh"
 #include "sf_internal.h"
@@ -347,11 +348,34 @@ __host__ __device__ constexpr size_t gather_header_bytes(int slots) {
            128 * 128;
 }
 
+// The EPV elements of a 16-byte chunk as fp32. A bf16 is the upper half of its fp32 value, so
+// each conversion is one shift or mask of the 32-bit word holding two of them.
+template <typename RT>
+__device__ __forceinline__ void chunk_to_f32(const uint4 &u, float (&x)[16 / sizeof(RT)]) {
+    if constexpr (sizeof(RT) == 4) {
+        x[0] = __uint_as_float(u.x), x[1] = __uint_as_float(u.y);
+        x[2] = __uint_as_float(u.z), x[3] = __uint_as_float(u.w);
+    } else if constexpr (std::is_same<RT, __nv_bfloat16>::value) {
+        x[0] = __uint_as_float(u.x << 16), x[1] = __uint_as_float(u.x & 0xffff0000u);
+        x[2] = __uint_as_float(u.y << 16), x[3] = __uint_as_float(u.y & 0xffff0000u);
+        x[4] = __uint_as_float(u.z << 16), x[5] = __uint_as_float(u.z & 0xffff0000u);
+        x[6] = __uint_as_float(u.w << 16), x[7] = __uint_as_float(u.w & 0xffff0000u);
+    } else {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h[i]);
+            x[2 * i] = f.x;
+            x[2 * i + 1] = f.y;
+        }
+    }
+}
+
 // Consumer warps a launch may have: with 3 or 4 chunks per thread the register budget allows 8.
 __host__ __device__ constexpr int gather_max_warps(int cpt) { return cpt >= 3 ? 8 : kGatherMaxWarps; }
 
 template <typename RT, int CPT, bool DOT>
-__global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_kernel(const GatherArgs g) {
+__global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT)), 1) csc_gather_kernel(const GatherArgs g) {
     constexpr int EPV = 16 / sizeof(RT);
     extern __shared__ __align__(128) unsigned char smem[];
     const int S = g.slots, G = g.group, NS = S / G;  // slots, rows per stage, stages
@@ -642,11 +666,7 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
         if constexpr (DOT) {  // only the dot products put rows of W in the stream
             if (m.z == 1) {
 #pragma unroll
-                for (int k = 0; k < CPT; ++k) {
-                    const RT *el = reinterpret_cast<const RT *>(&u[k]);
-#pragma unroll
-                    for (int e = 0; e < EPV; ++e) wv[k][e] = to_f32(el[e]);
-                }
+                for (int k = 0; k < CPT; ++k) chunk_to_f32<RT>(u[k], wv[k]);
                 return 0.f;
             }
         }
@@ -654,12 +674,12 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT))) csc_gather_k
         float dp = 0.f;
 #pragma unroll
         for (int k = 0; k < CPT; ++k) {
-            const RT *el = reinterpret_cast<const RT *>(&u[k]);
+            float x[EPV];
+            chunk_to_f32<RT>(u[k], x);
 #pragma unroll
             for (int e = 0; e < EPV; ++e) {
-                const float x = to_f32(el[e]);
-                acc[k][e] = fmaf(vf, x, acc[k][e]);
-                if constexpr (DOT) dp = fmaf(x, wv[k][e], dp);
+                acc[k][e] = fmaf(vf, x[e], acc[k][e]);
+                if constexpr (DOT) dp = fmaf(x[e], wv[k][e], dp);
             }
         }
         if (sums) vsum += (double)vf;
