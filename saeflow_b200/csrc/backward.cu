@@ -301,9 +301,8 @@ __device__ __forceinline__ bool mbar_wait_suspend(uint64_t *bar, uint32_t parity
 // range order. A column without entries is written as zeros by the range in which its (empty)
 // entry span starts.
 constexpr int kGatherMaxPieceBytes = 16384;
-constexpr int kGatherCtasPerSm = 2;
-constexpr int kGatherRingBytes = 192 * 1024 / kGatherCtasPerSm;
-constexpr int kGatherStages = 4;
+constexpr int kGatherSmemPerSm = 192 * 1024;  // rings of the CTAs an SM holds
+constexpr int kGatherStages = 2;
 constexpr int kGatherMaxWarps = 16;    // consumer warps
 constexpr int kGatherMinEntries = 64;  // entries per range at least
 
@@ -1027,12 +1026,14 @@ GatherPlan plan_gather(int64_t nnz, int64_t D, size_t es, bool aligned, bool dot
     p.slot_stride = (uint32_t)((std::max<int64_t>(p.piece_elems * (int64_t)es, (int64_t)p.consumer_warps * 32 * p.cpt * 16) + 127) /
                                128 * 128);
     int slots = 2;
-    while (slots < 64 && gather_header_bytes(slots + 1) + (size_t)(slots + 1) * p.slot_stride <= kGatherRingBytes)
-        ++slots;
+    // Three CTAs per SM without dot products; with them, the ten-warp CTAs run two per SM.
+    const int ctas_per_sm = dot ? 2 : 3;
+    const size_t ring_bytes = (size_t)kGatherSmemPerSm / ctas_per_sm;
+    while (slots < 64 && gather_header_bytes(slots + 1) + (size_t)(slots + 1) * p.slot_stride <= ring_bytes) ++slots;
     p.group = std::min(32, std::max(1, slots / kGatherStages));
     p.slots = slots / p.group * p.group;
     p.smem = gather_header_bytes(p.slots) + (size_t)p.slots * p.slot_stride;
-    const int64_t max_ranges = kGatherCtasPerSm * (int64_t)num_sms();
+    const int64_t max_ranges = ctas_per_sm * (int64_t)num_sms();
     int64_t ranges = std::min<int64_t>(max_ranges, (nnz + kGatherMinEntries - 1) / kGatherMinEntries);
     ranges = std::max<int64_t>(ranges, 1);
     p.per_range = (nnz + ranges - 1) / ranges;
