@@ -301,7 +301,7 @@ __device__ __forceinline__ bool mbar_wait_suspend(uint64_t *bar, uint32_t parity
 // range order. A column without entries is written as zeros by the range in which its (empty)
 // entry span starts.
 constexpr int kGatherMaxPieceBytes = 16384;
-constexpr int kGatherSmemPerSm = 192 * 1024;  // rings of the CTAs an SM holds
+constexpr int kGatherSmemPerSm = 192 * 1024;  // rings of the three CTAs an SM holds
 constexpr int kGatherStages = 2;
 constexpr int kGatherMaxWarps = 16;    // consumer warps
 constexpr int kGatherMinEntries = 64;  // entries per range at least
@@ -998,7 +998,7 @@ struct GatherPlan {
     size_t smem, carry_bytes, info_bytes;
 };
 
-GatherPlan plan_gather(int64_t nnz, int64_t D, size_t es, bool aligned, bool dot) {
+GatherPlan plan_gather(int64_t nnz, int64_t D, size_t es, bool aligned) {
     GatherPlan p{};
     p.bulk = aligned && nnz > 0 && D > 0 && (D * (int64_t)es) % 16 == 0;
     if (!p.bulk) return p;
@@ -1009,15 +1009,12 @@ GatherPlan plan_gather(int64_t nnz, int64_t D, size_t es, bool aligned, bool dot
     p.n_pieces = (D + p.piece_elems - 1) / p.piece_elems;
     const int64_t chunks = p.piece_elems / epv;
     // 16-byte chunks per consumer thread. Every consumer warp walks every row in the ring, so
-    // fewer, wider warps cut the per-row overhead; with dots each row also costs every warp a
-    // shuffle reduction, which more warps hide better. Without dots: the fewest warps that leave
-    // under a quarter of the lanes idle; with dots: one chunk per thread.
+    // fewer, wider warps cut the per-row overhead: the fewest warps that leave under a quarter
+    // of the lanes idle.
     p.cpt = 1;
-    if (!dot) {
-        for (int cpt = 2; cpt <= 4; ++cpt) {
-            const int64_t warps = (chunks + 32 * cpt - 1) / (32 * cpt);
-            if (warps <= gather_max_warps(cpt) && warps * 32 * cpt * 3 < chunks * 4) p.cpt = cpt;
-        }
+    for (int cpt = 2; cpt <= 4; ++cpt) {
+        const int64_t warps = (chunks + 32 * cpt - 1) / (32 * cpt);
+        if (warps <= gather_max_warps(cpt) && warps * 32 * cpt * 3 < chunks * 4) p.cpt = cpt;
     }
     while ((chunks + 32 * p.cpt - 1) / (32 * p.cpt) > gather_max_warps(p.cpt)) ++p.cpt;
     p.consumer_warps = (int)((chunks + 32 * p.cpt - 1) / (32 * p.cpt));
@@ -1026,8 +1023,7 @@ GatherPlan plan_gather(int64_t nnz, int64_t D, size_t es, bool aligned, bool dot
     p.slot_stride = (uint32_t)((std::max<int64_t>(p.piece_elems * (int64_t)es, (int64_t)p.consumer_warps * 32 * p.cpt * 16) + 127) /
                                128 * 128);
     int slots = 2;
-    // Three CTAs per SM without dot products; with them, the ten-warp CTAs run two per SM.
-    const int ctas_per_sm = dot ? 2 : 3;
+    const int ctas_per_sm = 3;
     const size_t ring_bytes = (size_t)kGatherSmemPerSm / ctas_per_sm;
     while (slots < 64 && gather_header_bytes(slots + 1) + (size_t)(slots + 1) * p.slot_stride <= ring_bytes) ++slots;
     p.group = std::min(32, std::max(1, slots / kGatherStages));
@@ -1114,7 +1110,7 @@ int sf_csc_gather_workspace(int64_t nnz, const sf_matrix *R, size_t *bytes) {
     if (!R || !bytes) return set_error(SF_ERR_INVALID, "NULL argument");
     if (!valid_dtype(R->dtype)) return set_error(SF_ERR_INVALID, "bad dtype");
     if (nnz < 0 || R->cols < 0) return set_error(SF_ERR_INVALID, "negative extent");
-    const GatherPlan p = plan_gather(nnz, R->cols, dtype_size(R->dtype), true, false);
+    const GatherPlan p = plan_gather(nnz, R->cols, dtype_size(R->dtype), true);
     *bytes = p.bulk ? p.carry_bytes + p.info_bytes : 0;
     return SF_OK;
 }
@@ -1151,7 +1147,7 @@ int sf_csc_gather(const int64_t *col_ptr, int64_t n_cols, const int32_t *col_idx
     const size_t es = dtype_size(R->dtype), oes = dtype_size(out->dtype);
     const bool aligned = aligned16(R->data) && (R->stride_row * (int64_t)es) % 16 == 0 &&
                          (!dot || (aligned16(W->data) && (W->stride_row * (int64_t)es) % 16 == 0));
-    const GatherPlan p = plan_gather(nnz, D, es, aligned, dot);
+    const GatherPlan p = plan_gather(nnz, D, es, aligned);
     return by_dtype(R->dtype, [&](auto rtag) {
         using RT = decltype(rtag);
         if (!p.bulk) {
