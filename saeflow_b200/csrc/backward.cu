@@ -64,38 +64,57 @@ __global__ void csr_to_csc_kernel(const int64_t *__restrict__ indptr, int64_t M,
 }
 
 // Rows ascending within each column, so the column view (and every sum taken over it in
-// order) does not depend on the scatter's atomic timing. A column of at most 32 entries is
-// ranked by one warp (each lane counts the smaller rows by shuffles); longer ones are queued
-// for csc_sort_large_kernel.
+// order) does not depend on the scatter's atomic timing. A column of at most 128 entries is
+// ranked by one warp: each lane holds up to four of its rows and counts the smaller rows of the
+// column, broadcast one at a time by shuffles. Longer columns are queued for
+// csc_sort_large_kernel.
+constexpr int kSortWarpMax = 128;
 __global__ void csc_sort_small_kernel(const int64_t *__restrict__ col_ptr, int64_t n_cols,
                                       const int32_t *__restrict__ trow, const int64_t *__restrict__ tperm,
                                       int32_t *__restrict__ row_idx, int64_t *__restrict__ perm,
                                       int32_t *__restrict__ col_idx, int32_t *__restrict__ large) {
+    constexpr int Q = kSortWarpMax / 32;
     const int lane = lane_id();
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t j = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); j < n_cols; j += warps) {
         const int64_t p0 = col_ptr[j];
-        const int n = (int)min(col_ptr[j + 1] - p0, (int64_t)33);
-        if (n > 32) {
+        const int n = (int)min(col_ptr[j + 1] - p0, (int64_t)kSortWarpMax + 1);
+        if (n > kSortWarpMax) {
             if (lane == 0) large[1 + atomicAdd(large, 1)] = (int32_t)j;
             continue;
         }
-        const int32_t r = lane < n ? trow[p0 + lane] : INT32_MAX;
-        const int64_t e = lane < n ? tperm[p0 + lane] : 0;
-        int rank = 0;
-        for (int t = 0; t < n; ++t) {
-            const int32_t rt = __shfl_sync(0xffffffffu, r, t);
-            rank += (rt < r || (rt == r && t < lane)) ? 1 : 0;
+        int32_t r[Q];
+        int rank[Q];
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const int i = q * 32 + lane;
+            r[q] = i < n ? trow[p0 + i] : INT32_MAX;
+            rank[q] = 0;
         }
-        if (lane < n) {
-            row_idx[p0 + rank] = r;
-            perm[p0 + rank] = e;
-            if (col_idx != nullptr) col_idx[p0 + rank] = (int32_t)j;
+#pragma unroll
+        for (int qt = 0; qt < Q; ++qt) {
+            if (qt * 32 >= n) break;
+            const int m = min(32, n - qt * 32);
+            for (int t = 0; t < m; ++t) {
+                const int32_t rt = __shfl_sync(0xffffffffu, r[qt], t);
+                const int it = qt * 32 + t;
+#pragma unroll
+                for (int q = 0; q < Q; ++q) rank[q] += (rt < r[q] || (rt == r[q] && it < q * 32 + lane)) ? 1 : 0;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            const int i = q * 32 + lane;
+            if (i < n) {
+                row_idx[p0 + rank[q]] = r[q];
+                perm[p0 + rank[q]] = tperm[p0 + i];
+                if (col_idx != nullptr) col_idx[p0 + rank[q]] = (int32_t)j;
+            }
         }
     }
 }
 
-// Columns of more than 32 entries, one CTA each: mark the column's rows in a shared-memory
+// Columns of more than kSortWarpMax entries, one CTA each: mark the column's rows in a shared-memory
 // bitmap (a window of up to 32 * words rows at a time), prefix-count the bitmap's words, and
 // place each entry at its row's rank. A row present twice in a column (a malformed CSR) sets
 // bit 4 of the device error; the placement then stays inside the column.
@@ -1073,7 +1092,7 @@ int sf_csr_transpose(const int64_t *indptr, int64_t M, const int32_t *indices, i
     const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     int32_t *cnt = static_cast<int32_t *>(workspace);
     int32_t *cursor = cnt + n_cols;
-    int32_t *large = cursor + n_cols;  // [0] count, [1..] columns of more than 32 entries
+    int32_t *large = cursor + n_cols;  // [0] count, [1..] columns csc_sort_small_kernel leaves
     int64_t *tperm = reinterpret_cast<int64_t *>(static_cast<char *>(workspace) + transpose_ints(n_cols));
     int32_t *trow = reinterpret_cast<int32_t *>(tperm + nnz);
     int st = check_cuda(cudaMemsetAsync(cnt, 0, (size_t)(2 * n_cols + 1) * sizeof(int32_t), s), "memset counts");

@@ -80,6 +80,8 @@ def _random_csr(M, n_cols, density, full_cols=(), seed=3):
         M, n_cols, generator=g, device="cuda")
     for j in full_cols:  # columns with an entry in every row: they span several ranges
         dense[:, j] = torch.randn(M, generator=g, device="cuda")
+    if n_cols > 60:  # a column with an entry in every fourth row (ranked by one warp up to 128)
+        dense[::4, 60] = torch.randn((M + 3) // 4, generator=g, device="cuda")
     if M > 5:
         dense[5] = 0      # an empty row
     if n_cols > 13:
