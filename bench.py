@@ -333,8 +333,8 @@ def run_ours(args, rank, world, device):
                 getattr(sae, name).grad = None
             return out
         # forward 5 (4 for TopK); backward: count, scan, scatter, 2 in-column sorts, 2 x (gather, carry),
-        # 2 transposes, decode
-        launches_per_step = 17
+        # transpose of dW_enc, matvec for db_dec (x takes no gradient here)
+        launches_per_step = 16
     elif sharded is not None:
         n_chunks = (T + args.chunk_tokens - 1) // args.chunk_tokens
 

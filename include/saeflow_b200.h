@@ -271,6 +271,13 @@ SF_API int sf_csr_transpose(const int64_t *indptr, int64_t M, const int32_t *ind
 SF_API int sf_csr_sddmm(const int64_t *indptr, int64_t M, const int32_t *indices, const sf_matrix *G,
                         const sf_matrix *W, const void *values, int values_dtype, float *out, sf_stream stream);
 
+/*
+ * y[i] = sum_j A[i, j] * x[j] with fp32 x and y, fp32 sums in a fixed order; A [rows, cols] any
+ * dtype with unit column stride. With A = W_enc and x = the per-feature sums of dpre (db_enc),
+ * y is the sum of dx over the tokens, which db_dec needs, without forming dx.
+ */
+SF_API int sf_matvec(const sf_matrix *A, const float *x, float *y, sf_stream stream);
+
 /* Bytes of workspace sf_csc_gather needs for nnz entries gathering rows of R (0 when it needs none). */
 SF_API int sf_csc_gather_workspace(int64_t nnz, const sf_matrix *R, size_t *bytes);
 

@@ -67,6 +67,7 @@ SIGNATURES = {
     "sf_csr_transpose": (_c.c_int, [_P, _c.c_int64, _P, _c.c_int64, _c.c_int64, _P, _P, _P, _P, _P, _c.c_size_t,
                                     _P]),
     "sf_csr_sddmm": (_c.c_int, [_P, _c.c_int64, _P, _MP, _MP, _P, _c.c_int, _P, _P]),
+    "sf_matvec": (_c.c_int, [_MP, _P, _P, _P]),
     "sf_csc_gather_workspace": (_c.c_int, [_c.c_int64, _MP, _SIZE_P]),
     "sf_csc_gather": (_c.c_int, [_P, _c.c_int64, _P, _c.c_int64, _P, _P, _P, _c.c_int, _MP, _MP, _P, _MP, _P, _P,
                                  _c.c_size_t, _P]),

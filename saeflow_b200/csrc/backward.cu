@@ -999,6 +999,38 @@ __global__ void __launch_bounds__(256) transpose2_kernel(const IT *__restrict__ 
     }
 }
 
+// y[i] = sum_j A[i, j] * x[j] (fp32 x, fp32 sums in a fixed order): one CTA per row of A,
+// 16-byte loads when the rows allow them. With A = W_enc and x = the column sums of dpre it gives
+// sum over tokens of dx without forming dx.
+template <typename T>
+__global__ void __launch_bounds__(256) matvec_kernel(const T *__restrict__ A, int64_t rows, int64_t cols, int64_t lda,
+                                                     const float *__restrict__ x, float *__restrict__ y, int vec) {
+    constexpr int EPV = 16 / sizeof(T);
+    __shared__ float part[8];
+    const int64_t i = blockIdx.x;
+    const T *a = A + i * lda;
+    float sum = 0.f;
+    if (vec) {
+        for (int64_t c = (int64_t)threadIdx.x * EPV; c < cols; c += 256 * EPV) {
+            float v[EPV];
+            chunk_to_f32<T>(__ldg(reinterpret_cast<const uint4 *>(a + c)), v);
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) sum = fmaf(v[e], __ldg(x + c + e), sum);
+        }
+    } else {
+        for (int64_t c = threadIdx.x; c < cols; c += 256) sum = fmaf(to_f32(a[c]), __ldg(x + c), sum);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane_id() == 0) part[threadIdx.x >> 5] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < 8; ++w) t += part[w];
+        y[i] = t;
+    }
+}
+
 template <typename F>
 int by_dtype(int dt, F &&f) {
     if (dt == SF_F32) return f(float{});
@@ -1282,6 +1314,27 @@ int sf_transpose(const sf_matrix *in, const sf_matrix *out, sf_stream stream) {
                                                           out->stride_row);
             return check_cuda(cudaGetLastError(), "transpose launch");
         });
+    });
+}
+
+int sf_matvec(const sf_matrix *A, const float *x, float *y, sf_stream stream) {
+    if (!A) return set_error(SF_ERR_INVALID, "A is NULL");
+    if (!valid_dtype(A->dtype)) return set_error(SF_ERR_INVALID, "bad dtype");
+    if (A->rows < 0 || A->cols < 0) return set_error(SF_ERR_INVALID, "negative extent");
+    if (A->stride_col != 1) return set_error(SF_ERR_UNSUPPORTED, "A needs a unit column stride");
+    if (A->rows == 0) return SF_OK;
+    if (!y || (A->cols > 0 && (!x || !A->data))) return set_error(SF_ERR_INVALID, "NULL pointer");
+    if (A->rows > (int64_t)INT32_MAX) return set_error(SF_ERR_UNSUPPORTED, "too many rows");
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    return by_dtype(A->dtype, [&](auto tag) {
+        using T = decltype(tag);
+        const int64_t es = (int64_t)sizeof(T);
+        const int vec = (aligned16(A->data) && aligned16(x) && (A->stride_row * es) % 16 == 0 && (A->cols * es) % 16 == 0)
+                            ? 1
+                            : 0;
+        matvec_kernel<T><<<(unsigned)A->rows, 256, 0, s>>>(reinterpret_cast<const T *>(A->data), A->rows, A->cols,
+                                                          A->stride_row, x, y, vec);
+        return check_cuda(cudaGetLastError(), "matvec launch");
     });
 }
 

@@ -9,7 +9,8 @@ the gradient of x_hat = decode(encode(x)) needs on a CSR pattern:
   with the per-entry dot products of each gathered row with the column's row of a second
   matrix (the gradient at the active features) in the same pass;
 - csr_sddmm: those dot products alone, on the CSR pattern;
-- transpose: a tiled transpose with a dtype conversion.
+- transpose: a tiled transpose with a dtype conversion;
+- matvec: a matrix-vector product (the token sum of dx, from W_enc and the sums of dpre).
 """
 
 from __future__ import annotations
@@ -72,6 +73,20 @@ def csr_sddmm(indptr, indices, values, G, W):
                                     ctypes.byref(_abi.matrix(W, "W")), values.data_ptr(),
                                     _abi.dtype_code(values.dtype, "values"), out.data_ptr(), _abi.stream_of(dev)))
     return out
+
+
+def matvec(A, x):
+    """fp32 [A.shape[0]]: y[i] = sum_j A[i, j] * x[j] (x fp32), fp32 sums in a fixed order."""
+    dev = _abi.require_cuda(("A", A), ("x", x))
+    A = A if A.stride(-1) == 1 else A.contiguous()
+    x = x.to(torch.float32).contiguous()
+    if x.numel() != A.shape[1]:
+        raise ValueError(f"x has {x.numel()} elements, A has {A.shape[1]} columns")
+    y = torch.empty(A.shape[0], dtype=torch.float32, device=dev)
+    lib = _abi.load()
+    with torch.cuda.device(dev):
+        _abi.check(lib.sf_matvec(ctypes.byref(_abi.matrix(A, "A")), x.data_ptr(), y.data_ptr(), _abi.stream_of(dev)))
+    return y
 
 
 def csc_gather(col_ptr, row_idx, perm, col_idx, values, R, *, W=None, out_dtype=torch.float32, col_sums=False):

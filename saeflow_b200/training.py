@@ -16,7 +16,9 @@ taken in one fixed order and the gradients are the same from run to run):
     dpre     = g[row] . W_dec[col] at each active entry     } gathered rows of g
     dW_enc^T = per feature, sum of dpre * (x - b_dec)[row], db_enc = per feature sum of dpre
                                                               (a second csc_gather pass)
-    dx       = dpre @ W_enc^T (the CSR decode against W_enc^T), db_dec = sum_rows (g - dx)
+    dx       = dpre @ W_enc^T (the CSR decode against W_enc^T), db_dec = sum_rows (g - dx);
+               without a gradient for x, db_dec = sum_rows g - W_enc @ db_enc (matvec), and dx
+               is never formed
 (x - b_dec) is taken rounded to W_enc's dtype, the operand the encoder multiplied.
 """
 
@@ -27,7 +29,7 @@ from dataclasses import dataclass
 import torch
 
 from .kernels import sparse_decode
-from .kernels.backward import csc_gather, csr_sddmm, csr_transpose, transpose
+from .kernels.backward import csc_gather, csr_sddmm, csr_transpose, matvec, transpose
 
 
 @dataclass
@@ -71,19 +73,23 @@ class _SparseForward(torch.autograd.Function):
             dW_dec = csc_gather(*col, values, g, out_dtype=W_dec.dtype)
         elif need_dpre:
             dpre = csr_sddmm(indptr, indices, values, g, W_dec)
+        sums = None  # fp32 per-feature sums of dpre
         if need_we or need_be:
             if x.dtype == b_dec.dtype == W_enc.dtype:
                 xs = x - b_dec  # torch subtracts 16-bit operands in fp32 and rounds once, as below
             else:
                 xs = (x.float() - b_dec.float()).to(W_enc.dtype)
-            dW_enc_t, db_enc = csc_gather(*col, dpre, xs, out_dtype=W_enc.dtype, col_sums=True)
+            dW_enc_t, sums = csc_gather(*col, dpre, xs, out_dtype=W_enc.dtype, col_sums=True)
             dW_enc = transpose(dW_enc_t) if need_we else None
-            db_enc = db_enc.to(W_enc.dtype) if need_be else None
-        if need_x or need_bd:
+            db_enc = sums.to(W_enc.dtype) if need_be else None
+        if need_x or (need_bd and sums is None):
             dx = sparse_decode(indptr, indices, dpre, transpose(W_enc), None, out_dtype=torch.float32)
             if need_bd:
                 db_dec = (g.sum(0, dtype=torch.float32) - dx.sum(0)).to(b_dec.dtype)
             dx = dx.to(x.dtype) if need_x else None
+        elif need_bd:
+            # sum over tokens of dx = W_enc @ (per-feature sums of dpre): no dx, no W_enc^T
+            db_dec = (g.sum(0, dtype=torch.float32) - matvec(W_enc, sums)).to(b_dec.dtype)
         return dx, dW_enc, db_enc, dW_dec, db_dec, None, None, None
 
 

@@ -13,7 +13,7 @@ import torch
 import oracle
 from saeflow_b200 import training
 from saeflow_b200.kernels import csr_to_dense, device_error
-from saeflow_b200.kernels.backward import csc_gather, csr_sddmm, csr_transpose, transpose
+from saeflow_b200.kernels.backward import csc_gather, csr_sddmm, csr_transpose, matvec, transpose
 
 pytestmark = pytest.mark.gpu
 
@@ -49,10 +49,11 @@ def _reference_grads(sae, x, r, active):
 @pytest.mark.parametrize("activation", ["relu", "jumprelu", "topk"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("shape", [(37, 64, 300), (300, 128, 1000)])
-def test_backward_matches_autograd_on_the_active_set(activation, dtype, shape):
+@pytest.mark.parametrize("x_grad", [True, False])
+def test_backward_matches_autograd_on_the_active_set(activation, dtype, shape, x_grad):
     M, d_in, d_sae = shape
     sae = _sae(d_in, d_sae, activation, dtype, k=12 if activation == "topk" else None)
-    x = (torch.randn(M, d_in, device="cuda") * 1.5).to(dtype).requires_grad_(True)
+    x = (torch.randn(M, d_in, device="cuda") * 1.5).to(dtype).requires_grad_(x_grad)
     out = training.forward(sae, x)
     r = torch.randn(M, d_in, device="cuda")
     (out.float() * r).sum().backward()
@@ -65,6 +66,8 @@ def test_backward_matches_autograd_on_the_active_set(activation, dtype, shape):
     tol = 1e-4 if dtype == torch.float32 else 3e-2
     got = {"x": x.grad, "W_enc": sae.W_enc.grad, "b_enc": sae.b_enc.grad, "W_dec": sae.W_dec.grad,
            "b_dec": sae.b_dec.grad}
+    if not x_grad:
+        del want["x"]
     for name, w in want.items():
         g = got[name].float()
         assert g.shape == w.shape, name
@@ -204,3 +207,15 @@ def test_transpose_kernel(src, dst, shape):
     for extra in (5, 6):  # odd and even row pitch
         strided = torch.randn(shape[0], shape[1] + extra, device="cuda").to(src)[:, 2:2 + shape[1]]
         assert torch.equal(transpose(strided, dst), strided.t().to(dst))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("shape", [(1, 1), (37, 1000), (2304, 4096)])
+def test_matvec(dtype, shape):
+    A = torch.randn(*shape, device="cuda").to(dtype)
+    x = torch.randn(shape[1], device="cuda")
+    want = A.double() @ x.double()
+    torch.testing.assert_close(matvec(A, x), want.float(), atol=1e-4 * shape[1] ** 0.5, rtol=1e-4)
+    strided = torch.randn(shape[0], shape[1] + 3, device="cuda").to(dtype)[:, 1:1 + shape[1]]
+    torch.testing.assert_close(matvec(strided, x), (strided.double() @ x.double()).float(),
+                               atol=1e-4 * shape[1] ** 0.5, rtol=1e-4)
