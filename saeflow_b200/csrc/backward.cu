@@ -1010,8 +1010,29 @@ __global__ void __launch_bounds__(256) matvec_kernel(const T *__restrict__ A, in
     const int64_t i = blockIdx.x;
     const T *a = A + i * lda;
     float sum = 0.f;
-    if (vec) {
-        for (int64_t c = (int64_t)threadIdx.x * EPV; c < cols; c += 256 * EPV) {
+    if (vec) {  // four 16-byte chunks of the row (and their x) in flight per thread
+        constexpr int U = 4;
+        int64_t c = (int64_t)threadIdx.x * EPV;
+        for (; c + (U - 1) * 256 * EPV < cols; c += U * 256 * EPV) {
+            uint4 ua[U];
+            float4 xa[U][EPV / 4];
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const int64_t ck = c + (int64_t)k * 256 * EPV;
+                ua[k] = __ldg(reinterpret_cast<const uint4 *>(a + ck));
+#pragma unroll
+                for (int h = 0; h < EPV / 4; ++h) xa[k][h] = __ldg(reinterpret_cast<const float4 *>(x + ck) + h);
+            }
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                float v[EPV];
+                chunk_to_f32<T>(ua[k], v);
+                const float *xv = reinterpret_cast<const float *>(xa[k]);
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) sum = fmaf(v[e], xv[e], sum);
+            }
+        }
+        for (; c < cols; c += 256 * EPV) {
             float v[EPV];
             chunk_to_f32<T>(__ldg(reinterpret_cast<const uint4 *>(a + c)), v);
 #pragma unroll
