@@ -1052,6 +1052,56 @@ __global__ void __launch_bounds__(256) matvec_kernel(const T *__restrict__ A, in
     }
 }
 
+// 16-bit to 16-bit on 64 x 64 tiles with 16-byte loads and stores (extents and pitches
+// multiples of 8, 16-byte aligned): each thread moves two 8-element chunks each way.
+__device__ __forceinline__ float half_bits_to_f32(uint16_t h, bool bf) {
+    return bf ? __uint_as_float((uint32_t)h << 16) : __half2float(__ushort_as_half(h));
+}
+__device__ __forceinline__ uint32_t pack_f32_pair(float a, float b, bool bf) {
+    if (bf) {
+        const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<const uint32_t *>(&v);
+    }
+    const __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+__global__ void __launch_bounds__(256) transpose16_kernel(const uint16_t *__restrict__ in, int64_t rows, int64_t cols,
+                                                          int64_t ldi, bool in_bf, uint16_t *__restrict__ out,
+                                                          int64_t ldo, bool out_bf) {
+    __shared__ float tile[64][65];
+    const int64_t r0 = (int64_t)blockIdx.y * 64, c0 = (int64_t)blockIdx.x * 64;
+    const int t = threadIdx.x, q = t & 7, rr = t >> 3;  // chunk q of row rr (and rr + 32)
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int lr = rr + 32 * k;
+        const int64_t r = r0 + lr, c = c0 + 8 * q;
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (r < rows && c < cols) u = __ldg(reinterpret_cast<const uint4 *>(in + r * ldi + c));
+        tile[lr][8 * q + 0] = half_bits_to_f32((uint16_t)(u.x & 0xffffu), in_bf);
+        tile[lr][8 * q + 1] = half_bits_to_f32((uint16_t)(u.x >> 16), in_bf);
+        tile[lr][8 * q + 2] = half_bits_to_f32((uint16_t)(u.y & 0xffffu), in_bf);
+        tile[lr][8 * q + 3] = half_bits_to_f32((uint16_t)(u.y >> 16), in_bf);
+        tile[lr][8 * q + 4] = half_bits_to_f32((uint16_t)(u.z & 0xffffu), in_bf);
+        tile[lr][8 * q + 5] = half_bits_to_f32((uint16_t)(u.z >> 16), in_bf);
+        tile[lr][8 * q + 6] = half_bits_to_f32((uint16_t)(u.w & 0xffffu), in_bf);
+        tile[lr][8 * q + 7] = half_bits_to_f32((uint16_t)(u.w >> 16), in_bf);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int lc = rr + 32 * k;  // the input column = the output row
+        const int64_t orow = c0 + lc, oc = r0 + 8 * q;
+        if (orow < cols && oc < rows) {
+            uint4 v;
+            v.x = pack_f32_pair(tile[8 * q + 0][lc], tile[8 * q + 1][lc], out_bf);
+            v.y = pack_f32_pair(tile[8 * q + 2][lc], tile[8 * q + 3][lc], out_bf);
+            v.z = pack_f32_pair(tile[8 * q + 4][lc], tile[8 * q + 5][lc], out_bf);
+            v.w = pack_f32_pair(tile[8 * q + 6][lc], tile[8 * q + 7][lc], out_bf);
+            *reinterpret_cast<uint4 *>(out + orow * ldo + oc) = v;
+        }
+    }
+}
+
 template <typename F>
 int by_dtype(int dt, F &&f) {
     if (dt == SF_F32) return f(float{});
@@ -1316,6 +1366,17 @@ int sf_transpose(const sf_matrix *in, const sf_matrix *out, sf_stream stream) {
     const bool pairs = in->rows % 2 == 0 && in->cols % 2 == 0 && in->stride_row % 2 == 0 && out->stride_row % 2 == 0 &&
                        (reinterpret_cast<uintptr_t>(in->data) % (2 * ies)) == 0 &&
                        (reinterpret_cast<uintptr_t>(out->data) % (2 * oes)) == 0 && (in->rows + 63) / 64 <= 65535;
+    const bool chunks16 = ies == 2 && oes == 2 && in->rows % 8 == 0 && in->cols % 8 == 0 && in->stride_row % 8 == 0 &&
+                          out->stride_row % 8 == 0 && aligned16(in->data) && aligned16(out->data) &&
+                          (in->rows + 63) / 64 <= 65535;
+    if (chunks16) {
+        const dim3 g16((unsigned)((in->cols + 63) / 64), (unsigned)((in->rows + 63) / 64));
+        transpose16_kernel<<<g16, 256, 0, s>>>(static_cast<const uint16_t *>(in->data), in->rows, in->cols,
+                                               in->stride_row, in->dtype == SF_BF16,
+                                               static_cast<uint16_t *>(const_cast<void *>(out->data)),
+                                               out->stride_row, out->dtype == SF_BF16);
+        return check_cuda(cudaGetLastError(), "transpose launch");
+    }
     dim3 grid((unsigned)((in->cols + 31) / 32), (unsigned)((in->rows + 31) / 32));
     if (pairs) grid = dim3((unsigned)((in->cols + 63) / 64), (unsigned)((in->rows + 63) / 64));
     return by_dtype(in->dtype, [&](auto itag) {

@@ -197,8 +197,8 @@ def test_backward_is_deterministic():
 
 
 @pytest.mark.parametrize("src,dst", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
-                                     (torch.float16, torch.float32)])
-@pytest.mark.parametrize("shape", [(1, 1), (33, 70), (300, 4099), (64, 130), (130, 4098)])
+                                     (torch.float16, torch.float32), (torch.float16, torch.bfloat16)])
+@pytest.mark.parametrize("shape", [(1, 1), (33, 70), (300, 4099), (64, 130), (130, 4098), (64, 136), (264, 4096)])
 def test_transpose_kernel(src, dst, shape):
     x = torch.randn(*shape, device="cuda").to(src)
     got = transpose(x, dst)
@@ -207,6 +207,8 @@ def test_transpose_kernel(src, dst, shape):
     for extra in (5, 6):  # odd and even row pitch
         strided = torch.randn(shape[0], shape[1] + extra, device="cuda").to(src)[:, 2:2 + shape[1]]
         assert torch.equal(transpose(strided, dst), strided.t().to(dst))
+    padded = torch.randn(shape[0], shape[1] + 8, device="cuda").to(src)[:, :shape[1]]  # aligned, pitch + 8
+    assert torch.equal(transpose(padded, dst), padded.t().to(dst))
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
