@@ -633,21 +633,51 @@ def cpu_step(ref, x):
     return torch.addmm(ref.b_dec32.expand(x.shape[0], -1), csr32, ref.W_dec32).to(ref.W_dec.dtype)
 
 
+def cpu_model():
+    """The host CPU's model name (from /proc/cpuinfo), for the baseline record."""
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def time_cpu(fn, budget_s):
+    """Runs fn until `budget_s` seconds have passed (at least once): (iterations, seconds)."""
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        fn()
+        n += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    return n, time.perf_counter() - t0
+
+
+def cpu_dense_forward_row(ref, x, budget_s):
+    """The second CPU row: the reference's dense SAE.forward, decode(encode(x)) with the dense
+    [M, d_sae] features and a dense product with W_dec (saeflow/reference.py:51-52)."""
+    ref.forward(x[:16])  # warm-up
+    n, dt = time_cpu(lambda: ref.forward(x), budget_s)
+    return {"value": round(n * x.shape[0] / dt, 1), "unit": "tokens/s",
+            "sample": f"{n} x {x.shape[0]} tokens in {dt:.1f} s (oracle restatement of saeflow.reference.SAE.forward)"}
+
+
 def cpu_baseline(cfg_id, budget_s=10.0, sample_tokens=None):
     cores = torch.get_num_threads()
     ref, x = cpu_pipeline_setup(cfg_id, sample_tokens or (1024 if cfg_id != 1 else 4096))
     cpu_step(ref, x[:64])  # warm-up
-    t0 = time.perf_counter()
-    n = 0
-    while True:
-        cpu_step(ref, x)
-        n += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = time.perf_counter() - t0
+    n, dt = time_cpu(lambda: cpu_step(ref, x), budget_s)
     return {"value": round(n * x.shape[0] / dt, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "cpu_model": cpu_model(), "logical_cpus": os.cpu_count(),
             "sample": f"{n} x {x.shape[0]} tokens of {CONFIGS[cfg_id]['name']} in {dt:.1f} s "
-                      "(oracle restatement of the reference CPU path: dense encode -> to_sparse_csr -> addmm)"}
+                      "(oracle restatement of the reference CPU path: dense encode -> to_sparse_csr -> addmm)",
+            "dense_forward": cpu_dense_forward_row(ref, x, budget_s / 2)}
 
 
 def run_reference_triton(args, device):
@@ -727,7 +757,8 @@ def run_reference(args):
         "config": {"workload": c["name"], "tokens_per_step": sample, "parallelism": "host CPU, rank 0 only"},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": desc},
+                         "cpu_model": cpu_model(), "logical_cpus": os.cpu_count(), "sample": desc,
+                         "dense_forward": cpu_dense_forward_row(ref, x, args.cpu_seconds / 2)},
         "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 

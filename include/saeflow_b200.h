@@ -206,11 +206,16 @@ SF_API int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *ind
  * The workspace is a 16 MiB array in the library's device image (held by every GPU that
  * loads the library's device code, until exit); this call allocates nothing. Operands
  * whose sf_fused_encode_workspace exceeds 16 MiB are rejected with SF_ERR_WORKSPACE
- * (e.g. bf16 x with d_in=2304: at most 3640 rows per call). The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) and should come before any
- * stream capture. Every call on a device shares the one array: calls whose kernels
- * overlap on the GPU (other streams, other host threads) race on it; serialise them.
- * Arguments and results are those of sf_fused_encode.
+ * (e.g. bf16 x with d_in=2304: at most 3640 rows per call). W_enc must be readable in
+ * place: a 16-bit W_enc contiguous along one dimension with a 16-byte-aligned base and
+ * row pitch, or on the TF32 path an fp32 W_enc in column-major layout (or the IEEE fp32
+ * path, which never copies W_enc); other layouts need a repacked copy of W_enc that the
+ * scratch cannot hold, and are rejected with their own message. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) and should come
+ * before any stream capture; the address is kept for the process's life, so calls after
+ * a cudaDeviceReset of that device are unsupported. Every call on a device shares the one
+ * array: calls whose kernels overlap on the GPU (other streams, other host threads) race
+ * on it; serialise them. Arguments and results are those of sf_fused_encode.
  */
 SF_API int sf_fused_encode_noalloc(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
                                    const sf_vector *b_dec, const sf_vector *threshold, int activation,

@@ -19,5 +19,6 @@ from .sae_oracle import (  # noqa: F401
     forward,
     fused_encode,
     sparse_decode,
+    to_dtype,
     topk_encode,
 )

@@ -58,40 +58,58 @@ class RefSAE(nn.Module):
         return self.decode(self.encode(x))
 
 
-def _shifted(x, b_dec, w_dtype):
+def to_dtype(t, dtype, rounding="nearest"):
+    """fp32 -> `dtype`. rounding="truncate" reproduces Triton's CPU interpreter, which
+    converts fp32 to bf16 by dropping the low 16 bits (the reference's golden vectors were
+    made under it); compiled Triton on a GPU, like these kernels, rounds to nearest even."""
+    if rounding == "truncate" and dtype == torch.bfloat16:
+        return (t.float().contiguous().view(torch.int32) & ~0xFFFF).view(torch.float32).to(torch.bfloat16)
+    if rounding not in ("nearest", "truncate"):
+        raise ValueError(f"rounding must be 'nearest' or 'truncate', got {rounding!r}")
+    return t.to(dtype)
+
+
+def _shifted(x, b_dec, w_dtype, rounding="nearest"):
     """(x - b_dec) in fp32, rounded to W_enc's dtype: the reference kernel prologue
-    (saeflow/kernels/encode.py:189, `(x.to(fp32) - b_dec.to(fp32)).to(w.dtype)`)."""
+    (saeflow/kernels/encode.py:72, `(x.to(fp32) - b_dec.to(fp32)).to(w.dtype)`)."""
     xs = x.float()
     if b_dec is not None:
         xs = xs - b_dec.float()
-    return xs.to(w_dtype)
+    return to_dtype(xs, w_dtype, rounding)
 
 
-def encode_pre(x, W_enc, b_enc, b_dec, chunk=4096):
-    """fp32 pre-activation acc + b_enc (encode.py:176-195), products summed in float64."""
-    xs = _shifted(x, b_dec, W_enc.dtype).double()
-    W = W_enc.double()
+def encode_pre(x, W_enc, b_enc, b_dec, chunk=4096, col_chunk=16384, rounding="nearest"):
+    """fp32 pre-activation acc + b_enc (encode.py:62-77), products summed in float64.
+
+    W_enc is widened to float64 one block of `col_chunk` columns at a time, so a large SAE
+    (4096 x 131072) needs no float64 copy of the whole matrix."""
+    xs = _shifted(x, b_dec, W_enc.dtype, rounding).double()
     b = b_enc.float()
-    out = torch.empty(x.shape[0], W_enc.shape[1], dtype=torch.float32)
-    for i in range(0, x.shape[0], chunk):
-        out[i:i + chunk] = (xs[i:i + chunk] @ W).float() + b
+    N = W_enc.shape[1]
+    out = torch.empty(x.shape[0], N, dtype=torch.float32)
+    for c0 in range(0, N, col_chunk):
+        c1 = min(N, c0 + col_chunk)
+        W = W_enc[:, c0:c1].double()
+        for i in range(0, x.shape[0], chunk):
+            out[i:i + chunk, c0:c1] = (xs[i:i + chunk] @ W).float() + b[c0:c1]
     return out
 
 
-def fused_encode(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", out_dtype=None):
-    """(out, row_nnz, pre) of the reference fused encoder (encode.py:195-208).
+def fused_encode(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", out_dtype=None, rounding="nearest"):
+    """(out, row_nnz, pre) of the reference fused encoder (encode.py:77-91).
 
     out = max(pre, 0), zeroed where not (pre > threshold) for JumpReLU, stored in
-    `out_dtype or x.dtype`; row_nnz counts the stored nonzeros (int32)."""
+    `out_dtype or x.dtype`; row_nnz counts the stored nonzeros (int32). `rounding` is the
+    fp32 -> bf16 conversion of the shifted input and of the output (see to_dtype)."""
     if activation not in ("relu", "jumprelu"):  # encode.py:107-108
         raise ValueError(f"fused_encode supports ['relu', 'jumprelu'], got {activation!r}")
     if activation == "jumprelu" and threshold is None:  # encode.py:109-110
         raise ValueError("jumprelu needs a threshold")
-    pre = encode_pre(x, W_enc, b_enc, b_dec)
+    pre = encode_pre(x, W_enc, b_enc, b_dec, rounding=rounding)
     out = torch.clamp_min(pre, 0.0)
     if activation == "jumprelu":
         out = torch.where(pre > threshold.float(), out, torch.zeros((), dtype=out.dtype))
-    out = out.to(out_dtype or x.dtype)
+    out = to_dtype(out, out_dtype or x.dtype, rounding)
     row_nnz = (out.float() != 0).sum(dim=1).to(torch.int32)
     return out, row_nnz, pre
 
@@ -113,19 +131,23 @@ def dense_to_csr(f, row_nnz=None):
     return torch.from_numpy(indptr), torch.from_numpy(cols.astype(np.int32)), values
 
 
-def sparse_decode(indptr, indices, values, W_dec, b_dec=None, out_dtype=None, chunk=1 << 20):
-    """b_dec + sum_j values[j] * W_dec[indices[j]] per row (decode.py:28-55), float64 sums."""
+def sparse_decode(indptr, indices, values, W_dec, b_dec=None, out_dtype=None):
+    """b_dec + sum_j values[j] * W_dec[indices[j]] per row (decode.py:28-55), float64 sums.
+
+    The row sums are one float64 CSR x dense product (the sum order does not matter at
+    float64 precision for these checks); only indptr's ranges of indices / values are read."""
     M = indptr.numel() - 1
-    D = W_dec.shape[1]
-    acc = torch.zeros(M, D, dtype=torch.float64)
+    D, N = W_dec.shape[1], W_dec.shape[0]
     ip = indptr.long()
-    rows = torch.repeat_interleave(torch.arange(M), ip[1:] - ip[:-1])
-    idx = indices.long()
-    vals = values.double()
-    Wd = W_dec.double()
-    for s in range(0, idx.numel(), chunk):
-        e = s + chunk
-        acc.index_add_(0, rows[s:e], vals[s:e, None] * Wd[idx[s:e]])
+    nnz = int(ip[-1]) if M else 0
+    acc = torch.zeros(M, D, dtype=torch.float64)
+    if nnz:
+        idx = indices[:nnz].long()
+        if int(idx.min()) < 0 or int(idx.max()) >= N:
+            raise ValueError("sparse_decode: an index is outside W_dec's rows")
+        with torch.sparse.check_sparse_tensor_invariants(False):
+            csr = torch.sparse_csr_tensor(ip, idx, values[:nnz].double(), (M, N))
+            acc += torch.sparse.mm(csr, W_dec.double())
     if b_dec is not None:
         acc += b_dec.double()
     return acc.to(out_dtype or W_dec.dtype)

@@ -25,7 +25,9 @@ std::mutex g_scratch_mu;
 
 // Device address of g_noalloc_scratch on the current device. In host code the array's
 // name is only a host-side stand-in, so the address is looked up once per device, with
-// that device current, and cached.
+// that device current, and cached for the life of the process. cudaDeviceReset unloads
+// the library's device image and may move the array, so calls after a reset of that
+// device are unsupported.
 int scratch_address(void **out) {
     int dev = -1;
     int st = sf::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
@@ -53,11 +55,27 @@ SF_API int sf_fused_encode_noalloc(const sf_matrix *x, const sf_matrix *W_enc, c
     size_t need = 0;
     int st = sf_fused_encode_workspace(x, W_enc, allow_tf32, variant, &need);
     if (st) return st;
-    if (need > kScratchBytes)
+    if (need > kScratchBytes) {
+        // The workspace of a zero-row x is the repacked copy of W_enc alone: nonzero when the
+        // tensor-core kernel cannot read W_enc in place. Fewer rows cannot shrink that part.
+        sf_matrix x0 = *x;
+        x0.rows = 0;
+        size_t w_part = 0;
+        st = sf_fused_encode_workspace(&x0, W_enc, allow_tf32, variant, &w_part);
+        if (st) return st;
+        if (w_part + 256 > kScratchBytes)
+            return sf::set_error(SF_ERR_WORKSPACE,
+                                 "sf_fused_encode_noalloc: W_enc is in a layout the tensor-core kernel cannot read "
+                                 "in place, and its repacked copy (%zu bytes) does not fit the %zu-byte static "
+                                 "scratch. Pass a 16-bit W_enc contiguous along one dimension with a 16-byte-aligned "
+                                 "base and row pitch, or an fp32 W_enc in column-major layout for TF32, or call "
+                                 "sf_fused_encode with a workspace.",
+                                 w_part, kScratchBytes);
         return sf::set_error(SF_ERR_WORKSPACE,
                              "sf_fused_encode_noalloc needs %zu bytes of scratch for these operands; its static "
                              "scratch holds %zu bytes. Call it on fewer rows of x at a time.",
                              need, kScratchBytes);
+    }
     void *scratch = nullptr;
     st = scratch_address(&scratch);
     if (st) return st;

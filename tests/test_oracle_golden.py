@@ -132,3 +132,76 @@ def test_oracle_encode_errors():
         oracle.fused_encode(x, W, b, torch.zeros(4), activation="gelu")
     with pytest.raises(ValueError):
         oracle.fused_encode(x, W, b, torch.zeros(4), activation="jumprelu")
+
+
+@pytest.mark.parametrize("case", range(ENC.int("n")))
+def test_reference_outputs_meet_the_contract_tolerances(case):
+    """The contract's rules (oracle/contract.py: rtol 1e-2 bf16 / 1e-5 fp32 with small
+    absolute floors, 1e-3 cut band, exact CSR rows) hold between the reference's own
+    outputs and the oracle: the oracle is pinned to the reference at the tolerances the GPU
+    tests hold the kernels to."""
+    from oracle import contract
+
+    p = f"c{case}/"
+    act = ENC.str(p + "activation")
+    x, W, b_enc, b_dec = ENC.t(p + "x"), ENC.t(p + "W_enc"), ENC.t(p + "b_enc"), ENC.t(p + "b_dec")
+    thr = ENC.t(p + "threshold")
+    if ENC.has(p + "colmajor"):
+        W = W.T.contiguous().T
+    want = ENC.t(p + "out")
+    # The golden vectors come from Triton's CPU interpreter, which converts fp32 to bf16 by
+    # truncation; the oracle restates that conversion for the bf16 cases (the GPU kernels,
+    # like compiled Triton, round to nearest and are checked against the default oracle).
+    rounding = "truncate" if x.dtype == torch.bfloat16 else "nearest"
+    got, _, pre = oracle.fused_encode(x, W, b_enc, b_dec, thr, act, rounding=rounding)
+    near = contract.near_cut(pre, thr, act)
+    contract.assert_values_close(want[~near].float(), got[~near].float(), x.dtype, what="reference vs oracle")
+    clean = torch.nonzero(~near.any(dim=1)).flatten().tolist()
+    contract.assert_csr_rows_match(oracle.dense_to_csr(want), oracle.dense_to_csr(got), clean, x.dtype)
+
+
+def test_contract_cut_band_and_topk_ambiguity():
+    from oracle import contract
+
+    pre = torch.tensor([[0.0005, 0.5, 1.2], [0.3, -0.0002, 2.0]])
+    thr = torch.tensor([-1.0, 0.5004, 1.0])
+    # JumpReLU: the cut is max(threshold, 0); ReLU: the cut is 0
+    assert contract.near_cut(pre, thr, "jumprelu").tolist() == [[True, True, False], [False, False, False]]
+    assert contract.near_cut(pre, None, "relu").tolist() == [[True, False, False], [False, True, False]]
+    assert contract.clean_rows(pre, None, "relu").tolist() == [False, False]
+    # a bf16 rounding midpoint next to the k-th value makes a row ambiguous; a wide gap does not
+    mid = 1.0 + 2.0 ** -8  # halfway between the bf16 neighbours 1.0 and 1.0078125
+    rows = torch.tensor([[3.0, 2.0, mid, 0.1], [3.0, 2.0, 1.0, 0.1]])
+    assert contract.topk_ambiguous_rows(rows, 3, torch.bfloat16).tolist() == [True, False]
+    with pytest.raises(AssertionError, match="outside rtol"):
+        contract.assert_values_close(torch.tensor([1.02]), torch.tensor([1.0]), torch.bfloat16)
+    contract.assert_values_close(torch.tensor([1.0078125, 5e-5]), torch.tensor([1.0, 0.0]), torch.bfloat16)
+
+
+def test_bf16_golden_outputs_are_the_truncating_conversion_bit_for_bit():
+    """Every bf16 golden output away from the cut is reproduced bit for bit by the oracle
+    with the interpreter's truncating fp32 -> bf16 conversion, and not by round-to-nearest:
+    the one difference between the golden vectors and the GPU contract is that rounding mode."""
+    from oracle import contract
+
+    n_trunc_diff = n_rn_diff = 0
+    for case in range(ENC.int("n")):
+        p = f"c{case}/"
+        x = ENC.t(p + "x")
+        if x.dtype != torch.bfloat16:
+            continue
+        act = ENC.str(p + "activation")
+        W, b_enc, b_dec, thr = ENC.t(p + "W_enc"), ENC.t(p + "b_enc"), ENC.t(p + "b_dec"), ENC.t(p + "threshold")
+        if ENC.has(p + "colmajor"):
+            W = W.T.contiguous().T
+        want = ENC.t(p + "out").view(torch.int16)
+        tr, _, pre = oracle.fused_encode(x, W, b_enc, b_dec, thr, act, rounding="truncate")
+        rn, _, _ = oracle.fused_encode(x, W, b_enc, b_dec, thr, act)
+        # a truncation boundary within fp32 summation error of pre is the only other way to differ
+        edge = (oracle.to_dtype(pre - 1e-5, torch.bfloat16, "truncate") !=
+                oracle.to_dtype(pre + 1e-5, torch.bfloat16, "truncate"))
+        keep = ~contract.near_cut(pre, thr, act) & ~edge
+        n_trunc_diff += int((tr.view(torch.int16) != want)[keep].sum())
+        n_rn_diff += int((rn.view(torch.int16) != want)[keep].sum())
+    assert n_trunc_diff == 0
+    assert n_rn_diff > 0

@@ -13,12 +13,12 @@ import ctypes
 import pytest
 import torch
 
+from oracle import contract
 from saeflow_b200 import _abi
 
 pytestmark = pytest.mark.gpu
 
 SCRATCH_BYTES = 16 << 20
-RTOL = 3e-2  # bf16 tolerance of the kernel tests
 
 
 def _operands(M, K, N, seed):
@@ -71,7 +71,7 @@ def test_noalloc_encode_matches_allocating_encode_on_two_calls():
         nnz = torch.zeros(M, device="cuda", dtype=torch.int32)
         _abi.check(_encode_noalloc(lib, x, W, b_enc, b_dec, thr, got, nnz))
         torch.cuda.synchronize()
-        torch.testing.assert_close(got.float(), want.float(), atol=RTOL, rtol=RTOL)
+        contract.assert_values_close(got.float().cpu(), want.float().cpu(), torch.bfloat16, what="no-alloc encode")
         assert torch.equal(nnz, want_nnz)
         assert torch.equal(nnz.cpu(), torch.count_nonzero(got, dim=1).int().cpu())
     assert _abi.device_error() == 0
@@ -89,3 +89,25 @@ def test_noalloc_encode_rejects_operands_beyond_its_scratch():
     assert b"scratch" in lib.sf_last_error()
     torch.cuda.synchronize()
     assert int(nnz.abs().sum()) == 0 and int(out.float().abs().sum()) == 0  # nothing ran
+
+
+def test_noalloc_encode_rejects_a_weight_layout_it_would_have_to_copy():
+    """An fp32 row-major W_enc on the TF32 path must be repacked K-major; at 2304 x 16384
+    that copy alone is 151 MB, so fewer rows cannot help and the message says what layout
+    to pass instead."""
+    lib = _abi.load()
+    K, N, M = 2304, 16384, 8
+    g = torch.Generator(device="cuda").manual_seed(14)
+    x = torch.randn(M, K, generator=g, device="cuda")
+    W = torch.randn(K, N, generator=g, device="cuda")  # row-major fp32: not K-major
+    b_enc, b_dec = torch.zeros(N, device="cuda"), torch.zeros(K, device="cuda")
+    out = torch.zeros(M, N, device="cuda")
+    xm, wm, be, bd, om = (_abi.matrix(x, "x"), _abi.matrix(W, "W_enc"), _abi.vector(b_enc, "b_enc"),
+                          _abi.vector(b_dec, "b_dec"), _abi.matrix(out, "out"))
+    st = lib.sf_fused_encode_noalloc(ctypes.byref(xm), ctypes.byref(wm), ctypes.byref(be), ctypes.byref(bd), None,
+                                     _abi.SF_ACT_RELU, ctypes.byref(om), None, 1, 0, _abi.stream_of(x.device))
+    assert st == _abi.SF_ERR_WORKSPACE
+    msg = lib.sf_last_error()
+    assert b"layout" in msg and b"column-major" in msg
+    torch.cuda.synchronize()
+    assert int(out.abs().sum()) == 0  # nothing ran
