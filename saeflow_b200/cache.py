@@ -1,8 +1,8 @@
 """Activation caching with on-the-fly SAE encoding: a drop-in for saeflow/cache.py.
 
-The directory layout, manifest, shard atomicity, resume rule and reader are the
-reference's (saeflow/cache.py:1-14, :39-45, :70-137, :140-194), because other tools read
-this format:
+The on-disk format, the manifest, the resume rule and the reader's batches are the
+reference's (saeflow/cache.py:1-14, :70-137, :140-194), because other tools read this
+format; the code that writes and reads it is this package's own:
 
     manifest.json                                   config + list of finished shards
     <hook>/<shard:05d>.npy                          dense activations [rows, d]
@@ -40,7 +40,6 @@ from __future__ import annotations
 import json
 import os
 import queue
-import re
 import threading
 from pathlib import Path
 
@@ -61,42 +60,70 @@ def _encode_sparse(sae, x):
 
 # ----------------------------------------------------------------------------- host side
 
-def _to_numpy(t: torch.Tensor) -> np.ndarray:
-    t = t.detach().contiguous().cpu()
-    return (t.view(torch.int16) if t.dtype == torch.bfloat16 else t).numpy()
+def _npy_view(t: torch.Tensor) -> np.ndarray:
+    """The array a shard file stores for `t`: its values on the host, bf16 as the raw int16
+    bit patterns (numpy has no bf16; the manifest's dtype says how to read them back)."""
+    host = t.detach().cpu().contiguous()
+    if host.dtype == torch.bfloat16:
+        host = host.view(torch.int16)
+    return host.numpy()
 
 
-def _from_numpy(a, dtype) -> torch.Tensor:
-    t = torch.from_numpy(np.array(a))  # a copy: the shard arrays are read-only memory maps
-    return t.view(dtype) if dtype == torch.bfloat16 else t
+def _tensor_of(arr: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
+    """A writable tensor holding a (read-only, memory-mapped) stored array, bf16 restored."""
+    t = torch.from_numpy(np.array(arr, copy=True))
+    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
 
 
-def _atomic_write(path: Path, write) -> None:
-    tmp = path.with_name(path.name + ".tmp")
-    with open(tmp, "wb") as fh:
-        write(fh)
+def _publish(path: Path, payload) -> None:
+    """Write a file so that readers see either nothing or all of it: `payload(fh)` writes a
+    sibling `<name>.partial`, which is flushed to stable storage before it is renamed over
+    `path`; the directory is then synced so the rename itself survives a crash."""
+    staging = path.parent / (path.name + ".partial")
+    with open(staging, "wb") as fh:
+        payload(fh)
         fh.flush()
         os.fsync(fh.fileno())
-    os.replace(tmp, path)
+    os.replace(staging, path)
+    try:
+        dir_fd = os.open(path.parent, os.O_RDONLY)
+    except OSError:  # a filesystem without directory handles
+        return
+    try:
+        os.fsync(dir_fd)
+    except OSError:
+        pass
+    finally:
+        os.close(dir_fd)
 
 
-def _save(path: Path, t: torch.Tensor) -> None:
-    _atomic_write(path, lambda fh: np.save(fh, _to_numpy(t)))
+def _write_npy(path: Path, t: torch.Tensor) -> None:
+    """One shard array as a .npy file (the format np.save writes), published atomically."""
+    arr = _npy_view(t)
+    _publish(path, lambda fh: np.lib.format.write_array(fh, arr, allow_pickle=False))
 
 
-def _cat_csr(parts):
-    """Row-wise concatenation of CSR blocks (indptr rebased onto one running offset)."""
-    indptrs, offset = [torch.zeros(1, dtype=torch.int64)], 0
-    for indptr, _, _ in parts:
-        indptrs.append(indptr[1:].cpu().to(torch.int64) + offset)
-        offset += int(indptr[-1])
-    return (torch.cat(indptrs), torch.cat([p[1].cpu() for p in parts]), torch.cat([p[2].cpu() for p in parts]))
+def _stack_csr(blocks):
+    """Row blocks of CSR (indptr, indices, values) stacked into one CSR: the per-row counts
+    of every block, in order, summed into one indptr."""
+    counts = torch.cat([ip[1:].to(torch.int64) - ip[:-1].to(torch.int64) for ip, _, _ in blocks])
+    indptr = torch.zeros(counts.numel() + 1, dtype=torch.int64)
+    torch.cumsum(counts, 0, out=indptr[1:])
+    return indptr, torch.cat([ix for _, ix, _ in blocks]), torch.cat([vs for _, _, vs in blocks])
 
 
-def _stop_layer(hook_names):
-    """Blocks the forward needs for the deepest requested hook (None: run them all)."""
-    layers = [re.match(r"blocks\.(\d+)\.", h) for h in hook_names]
-    return max(int(m.group(1)) for m in layers) + 1 if all(layers) else None
+def _layers_to_run(hook_names):
+    """How many transformer blocks the forward must run to reach every hook: one past the
+    deepest `blocks.<n>.` hook, or None (run the whole model) when any hook lives outside
+    the blocks (embeddings, final norm) or no hook is named."""
+    deepest = None
+    for name in hook_names:
+        prefix, _, rest = name.partition(".")
+        layer, dot, _ = rest.partition(".")
+        if prefix != "blocks" or not dot or not (layer.isascii() and layer.isdigit()):
+            return None
+        deepest = max(int(layer), -1 if deepest is None else deepest)
+    return None if deepest is None else deepest + 1
 
 
 # ----------------------------------------------------------------------------- async copies
@@ -169,18 +196,18 @@ class _ShardWriter:
     def _write(self, shard: int, parts: dict, hooks_meta: dict, n_seqs: int, n_rows: int) -> None:
         for h, pieces in parts.items():
             if hooks_meta[h]["format"] == "csr":
-                csr = _cat_csr([tuple(c.wait() for c in piece) for piece in pieces])
+                csr = _stack_csr([tuple(c.wait() for c in piece) for piece in pieces])
                 for name, t in zip(_CSR_PARTS, csr):
-                    _save(self.out_dir / h / f"{shard:05d}.{name}.npy", t)
+                    _write_npy(self.out_dir / h / f"{shard:05d}.{name}.npy", t)
             else:
-                _save(self.out_dir / h / f"{shard:05d}.npy", torch.cat([c.wait() for c in pieces]))
+                _write_npy(self.out_dir / h / f"{shard:05d}.npy", torch.cat([c.wait() for c in pieces]))
             self.manifest["hooks"][h] = hooks_meta[h]
         entry = {"n_seqs": n_seqs, "n_rows": n_rows}
         if self.index_shards:
             entry["index"] = shard
         self.manifest["shards"].append(entry)
         text = json.dumps(self.manifest, indent=2).encode()
-        _atomic_write(self.manifest_path, lambda fh: fh.write(text))
+        _publish(self.manifest_path, lambda fh: fh.write(text))
 
 
 # ----------------------------------------------------------------------------- writer API
@@ -199,7 +226,7 @@ def _run_shards(model, tokens, hook_names, out_dir, encoders, dtype, batch_size,
     """Compute shards [first, stop_shard) and hand them to a writer that records them in
     `manifest` / `manifest_path`."""
     device = next(model.parameters()).device
-    stop = _stop_layer(hook_names)
+    stop = _layers_to_run(hook_names)
     streams: dict = {}
     writer = _ShardWriter(out_dir, manifest, manifest_path, index_shards)
     try:
@@ -282,7 +309,7 @@ def cache_activations(model, tokens, hook_names, out_dir, *, batch_size=8, batch
     rank_manifest = _load_manifest(rank_path, {**config, "rank": rank, "world": world}, out_dir)
     if not rank_path.exists():  # recorded even when this rank's block is empty
         text = json.dumps(rank_manifest, indent=2).encode()
-        _atomic_write(rank_path, lambda fh: fh.write(text))
+        _publish(rank_path, lambda fh: fh.write(text))
     first = max(s0, done, max((e["index"] + 1 for e in rank_manifest["shards"]), default=s0))
     error = None
     try:
@@ -321,7 +348,7 @@ def _merge_rank_manifests(out_dir: Path, manifest: dict, manifest_path: Path, ho
     manifest["hooks"] = {h: manifest["hooks"][h] for h in hook_names if h in manifest["hooks"]}
     manifest["shards"] += [{"n_seqs": e["n_seqs"], "n_rows": e["n_rows"]} for e in entries]
     text = json.dumps(manifest, indent=2).encode()
-    _atomic_write(manifest_path, lambda fh: fh.write(text))
+    _publish(manifest_path, lambda fh: fh.write(text))
     for p in paths:
         p.unlink()
 
@@ -329,53 +356,81 @@ def _merge_rank_manifests(out_dir: Path, manifest: dict, manifest_path: Path, ho
 # ----------------------------------------------------------------------------- reader
 
 class ActivationReader:
-    """Streams a cache written by cache_activations (here or by saeflow) back as batches."""
+    """Streams a cache written by cache_activations (here or by saeflow) back as batches.
+
+    The shards of a hook are one sequence of rows: a row index built once from the
+    manifest (the first global row of every shard) locates any global row range, and
+    `read_rows` slices it out of the memory-mapped shard files, so batches of any size
+    cross shard boundaries without buffering rows. Same constructor, attributes and
+    batches as saeflow.cache.ActivationReader (cache.py:140-194)."""
 
     def __init__(self, path):
         self.path = Path(path)
         self.manifest = json.loads((self.path / "manifest.json").read_text())
         self.dtype = _DTYPES[self.manifest["config"]["dtype"]]
+        sizes = np.array([s["n_rows"] for s in self.manifest["shards"]], dtype=np.int64)
+        self._first_row = np.concatenate([[0], np.cumsum(sizes)])  # shard i holds [first[i], first[i+1])
+        self._maps: dict = {}
 
     @property
     def hook_names(self):
         return self.manifest["config"]["hook_names"]
 
     def n_rows(self):
-        return sum(s["n_rows"] for s in self.manifest["shards"])
+        """Rows (token positions) in the cache, per hook."""
+        return int(self._first_row[-1])
 
-    def _is_csr(self, hook):
+    def is_sparse(self, hook):
+        """True when `hook` was SAE-encoded on the fly and is stored as CSR features."""
         return self.manifest["hooks"][hook]["format"] == "csr"
 
-    def _open(self, hook, shard):
-        d = self.path / hook
-        if self._is_csr(hook):
-            return [np.load(d / f"{shard:05d}.{name}.npy", mmap_mode="r") for name in _CSR_PARTS]
-        return np.load(d / f"{shard:05d}.npy", mmap_mode="r")
+    def _shard_arrays(self, hook, i):
+        """Memory maps of shard i of `hook`, opened on first use."""
+        key = (hook, i)
+        if key not in self._maps:
+            d = self.path / hook
+            if self.is_sparse(hook):
+                self._maps[key] = tuple(np.load(d / f"{i:05d}.{part}.npy", mmap_mode="r") for part in _CSR_PARTS)
+            else:
+                self._maps[key] = np.load(d / f"{i:05d}.npy", mmap_mode="r")
+        return self._maps[key]
 
-    def _rows(self, hook, arrays, a, b):
-        if not self._is_csr(hook):
-            return _from_numpy(arrays[a:b], self.dtype)
-        indptr, indices, values = arrays
-        lo, hi = int(indptr[a]), int(indptr[b])
-        return (torch.from_numpy(np.array(indptr[a:b + 1]) - lo), torch.from_numpy(np.array(indices[lo:hi])),
-                _from_numpy(values[lo:hi], self.dtype))
-
-    def _join(self, hook, pieces):
-        return _cat_csr(pieces) if self._is_csr(hook) else torch.cat(pieces)
+    def read_rows(self, hook, start, stop):
+        """Global rows [start, stop) of `hook`: a [rows, d] tensor, or a CSR (indptr,
+        indices, values) tuple for an encoded hook, on the host."""
+        if not 0 <= start <= stop <= self.n_rows():
+            raise IndexError(f"rows [{start}, {stop}) outside the cache's {self.n_rows()} rows")
+        first = int(np.searchsorted(self._first_row, start, side="right")) - 1
+        last = int(np.searchsorted(self._first_row, stop, side="left"))
+        blocks = []
+        for i in range(max(first, 0), min(last, len(self.manifest["shards"]))):
+            lo = max(start, int(self._first_row[i])) - int(self._first_row[i])
+            hi = min(stop, int(self._first_row[i + 1])) - int(self._first_row[i])
+            if hi <= lo:
+                continue
+            arrays = self._shard_arrays(hook, i)
+            if self.is_sparse(hook):
+                indptr, indices, values = arrays
+                ip = np.array(indptr[lo:hi + 1], dtype=np.int64)
+                blocks.append((torch.from_numpy(ip), _tensor_of(indices[ip[0]:ip[-1]], torch.int32),
+                               _tensor_of(values[ip[0]:ip[-1]], self.dtype)))
+            else:
+                blocks.append(_tensor_of(arrays[lo:hi], self.dtype))
+        if self.is_sparse(hook):
+            if not blocks:
+                return (torch.zeros(1, dtype=torch.int64), torch.zeros(0, dtype=torch.int32),
+                        torch.zeros(0, dtype=self.dtype))
+            return _stack_csr(blocks)
+        if not blocks:
+            return torch.zeros(0, self.manifest["hooks"][hook]["d"], dtype=self.dtype)
+        return blocks[0] if len(blocks) == 1 else torch.cat(blocks)
 
     def _host_batches(self, hook, batch_size):
-        pending, n_pending = [], 0
-        for i, shard in enumerate(self.manifest["shards"]):
-            arrays, row = self._open(hook, i), 0
-            while row < shard["n_rows"]:
-                take = min(batch_size - n_pending, shard["n_rows"] - row)
-                pending.append(self._rows(hook, arrays, row, row + take))
-                n_pending, row = n_pending + take, row + take
-                if n_pending == batch_size:
-                    yield self._join(hook, pending)
-                    pending, n_pending = [], 0
-        if pending:
-            yield self._join(hook, pending)
+        if batch_size < 1:
+            raise ValueError("batch_size must be positive")
+        total = self.n_rows()
+        for start in range(0, total, batch_size):
+            yield self.read_rows(hook, start, min(total, start + batch_size))
 
     def iter_batches(self, hook, batch_size, device=None):
         """Yield `batch_size`-row batches in cache order (the last may be short), crossing

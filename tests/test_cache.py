@@ -78,6 +78,34 @@ def test_reader_reads_the_reference_caches(model, tokens):
     assert torch.equal(dense, sae.encode(cf.expected(model, tokens, cf.HOOKS[0])))
 
 
+def test_read_rows_is_random_access_across_shards():
+    """Any global row range, inside one shard or across several, equals the same rows of a
+    full read; empty ranges and ranges past the end behave."""
+    for name, hook in (("dense_fp32", cf.HOOKS[1]), ("csr_fp32", cf.HOOKS[0])):
+        reader = ActivationReader(GOLDEN / name)
+        n = reader.n_rows()
+        whole = reader.read_rows(hook, 0, n)
+        if reader.is_sparse(hook):
+            whole = csr_to_dense(*whole, 96)
+        for a, b in ((0, 1), (3, 3), (5, 70), (63, 65), (17, n), (n - 1, n), (n, n)):
+            got = reader.read_rows(hook, a, b)
+            if reader.is_sparse(hook):
+                assert got[0][0] == 0 and got[0].numel() == b - a + 1
+                got = csr_to_dense(*got, 96)
+            assert torch.equal(got, whole[a:b]), (name, a, b)
+        with pytest.raises(IndexError):
+            reader.read_rows(hook, 0, n + 1)
+        with pytest.raises(ValueError):
+            next(reader.iter_batches(hook, 0))
+
+
+def test_layers_to_run():
+    assert sf_cache._layers_to_run(["blocks.0.hook_resid_post", "blocks.11.attn.hook_z"]) == 12
+    assert sf_cache._layers_to_run(["blocks.2.hook_mlp_out", "hook_embed"]) is None
+    assert sf_cache._layers_to_run(["blocks.x.hook"]) is None
+    assert sf_cache._layers_to_run([]) is None
+
+
 # ------------------------------------------------------------------ the reference's cache tests
 
 def test_write_and_read_back_exactly(model, tokens, tmp_path):
@@ -95,7 +123,7 @@ def test_resume_after_interruption(model, tokens, tmp_path):
     cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
     reader = ActivationReader(tmp_path)
     assert len(reader.manifest["shards"]) == 3
-    assert not list(tmp_path.rglob("*.tmp"))
+    assert not list(tmp_path.rglob("*.partial"))
     for hook in cf.HOOKS:
         assert torch.equal(read_all(reader, hook, 5), cf.expected(model, tokens, hook))
 
@@ -132,7 +160,7 @@ def test_encode_on_the_fly_stores_sparse(model, tokens, tmp_path, cpu_encoder):
 # ------------------------------------------------------------------ the background writer
 
 def test_failed_shard_write_leaves_only_whole_shards_and_resumes(model, tokens, tmp_path, monkeypatch):
-    real_save, calls = sf_cache._save, []
+    real_save, calls = sf_cache._write_npy, []
 
     def flaky_save(path, t):
         calls.append(path)
@@ -140,11 +168,11 @@ def test_failed_shard_write_leaves_only_whole_shards_and_resumes(model, tokens, 
             raise OSError("disk full")
         real_save(path, t)
 
-    monkeypatch.setattr(sf_cache, "_save", flaky_save)
+    monkeypatch.setattr(sf_cache, "_write_npy", flaky_save)
     with pytest.raises(RuntimeError, match="writer failed"):
         cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
     assert len(ActivationReader(tmp_path).manifest["shards"]) == 1
-    monkeypatch.setattr(sf_cache, "_save", real_save)
+    monkeypatch.setattr(sf_cache, "_write_npy", real_save)
     cache_activations(model, tokens, cf.HOOKS, tmp_path, batch_size=4, batches_per_shard=2)
     same_tree(tmp_path, GOLDEN / "dense_fp32")
 
