@@ -9,12 +9,15 @@ code, shape, strides) and passes torch's current CUDA stream.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libsaeflow_b200.so"
+# The in-tree build; SAEFLOW_B200_LIB names another build of the same library (e.g. one
+# compiled with different tuning flags) to load instead.
+LIB_PATH = Path(os.environ.get("SAEFLOW_B200_LIB") or Path(__file__).resolve().parent / "_lib" / "libsaeflow_b200.so")
 
 SF_F32, SF_BF16, SF_F16 = 0, 1, 2
 DTYPE_CODES = {torch.float32: SF_F32, torch.bfloat16: SF_BF16, torch.float16: SF_F16}

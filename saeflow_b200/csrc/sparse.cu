@@ -8,6 +8,9 @@
 //   topk_merge_kernel  replaces torch.topk on the dense ReLU output (saeflow/ops.py:12-16)
 #include <algorithm>
 
+#include <cstring>
+#include <type_traits>
+
 #include "sf_common.cuh"
 #include "sf_internal.h"
 
@@ -249,16 +252,63 @@ __global__ void compact_kernel(const T *__restrict__ f, int64_t M, int64_t N, in
 // The slice width is chosen on the host so that one slice of every W_dec row fits in L2
 // (kDecodeL2Budget); the grid runs all rows of slice 0, then slice 1, ..., so each W_dec
 // row slice comes from HBM about once and its other uses hit L2.
+// The kernel is bound by instruction issue, not by L2 (ncu at config 2, 4096 tokens:
+// issue slots 75% busy, L2 throughput 37% of peak), so the per-element work is kept to
+// the fewest instructions: accumulators are fp32 pairs updated by one packed FMA
+// (__ffma2_rn, two IEEE fp32 FMAs, each bit-identical to fmaf) per two W elements, and
+// bf16 elements are widened by placing their bits in the high half of a 32-bit word (exact).
 #ifndef SF_DECODE_WPOL
 #define SF_DECODE_WPOL 0  // W_dec loads: 0 default L2 policy, 1 evict_last
 #endif
 #ifndef SF_DECODE_OPOL
 #define SF_DECODE_OPOL 1  // output stores: 0 default L2 policy, 1 evict_first
 #endif
+#ifndef SF_DECODE_MATH
+#define SF_DECODE_MATH 1  // 0 scalar fmaf per element; 1 packed fp32 FMA per element pair
+#endif
 __device__ __forceinline__ uint4 ld_w_v4(const void *p, uint64_t pol) {
     if (SF_DECODE_WPOL) return ld_nc_v4_hint(p, pol);
     return __ldg(reinterpret_cast<const uint4 *>(p));
 }
+
+// The two W elements of 32-bit word `w` of a gathered 16-bit vector, widened to fp32 (exact).
+template <typename WT>
+__device__ __forceinline__ float2 widen_pair(uint32_t w) {
+    if constexpr (std::is_same<WT, __nv_bfloat16>::value) {
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    } else {
+        __half2 h;
+        memcpy(&h, &w, 4);
+        return __half22float2(h);
+    }
+}
+
+// acc[v][i] += a * (elements 2i, 2i+1 of vector q[v]).
+template <typename WT, int V, int NP>
+__device__ __forceinline__ void fma_vectors(float2 (&acc)[V][NP], float a, const uint4 (&q)[V],
+                                            const bool (&active)[V]) {
+    const float2 aa = make_float2(a, a);
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        if (!active[v]) continue;
+        const uint32_t w[4] = {q[v].x, q[v].y, q[v].z, q[v].w};
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+            float2 wf;
+            if constexpr (sizeof(WT) == 4)
+                wf = make_float2(__uint_as_float(w[2 * i]), __uint_as_float(w[2 * i + 1]));
+            else
+                wf = widen_pair<WT>(w[i]);
+            if (SF_DECODE_MATH == 1) {
+                acc[v][i] = __ffma2_rn(aa, wf, acc[v][i]);
+            } else {
+                acc[v][i].x = fmaf(a, wf.x, acc[v][i].x);
+                acc[v][i].y = fmaf(a, wf.y, acc[v][i].y);
+            }
+        }
+    }
+}
+
 template <typename WT, typename VT, typename OT, int V>
 __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restrict__ indptr,
                                                          const int32_t *__restrict__ indices,
@@ -267,6 +317,7 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
                                                          int64_t b_stride, OT *__restrict__ out, int64_t ldo,
                                                          int64_t M, int64_t D, int out_vec, unsigned *err) {
     constexpr int EPV = 16 / sizeof(WT);
+    constexpr int NP = EPV / 2;  // element pairs per vector
     constexpr int SLICE = 32 * V * EPV;
     const int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
     if (row >= M) return;
@@ -274,11 +325,11 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
     const int64_t d0 = (int64_t)blockIdx.y * SLICE;
     const int64_t start = indptr[row], end = indptr[row + 1];
 
-    float acc[V][EPV];
+    float2 acc[V][NP];
 #pragma unroll
     for (int v = 0; v < V; ++v)
 #pragma unroll
-        for (int e = 0; e < EPV; ++e) acc[v][e] = 0.f;
+        for (int i = 0; i < NP; ++i) acc[v][i] = make_float2(0.f, 0.f);
 
     bool active[V];
 #pragma unroll
@@ -314,29 +365,17 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
                 q0[v] = active[v] ? ld_w_v4(r0 + v * 32 * EPV, wpol) : make_uint4(0, 0, 0, 0);
                 q1[v] = active[v] ? ld_w_v4(r1 + v * 32 * EPV, wpol) : make_uint4(0, 0, 0, 0);
             }
-#pragma unroll
-            for (int v = 0; v < V; ++v) {
-                const WT *e0 = reinterpret_cast<const WT *>(&q0[v]);
-                const WT *e1 = reinterpret_cast<const WT *>(&q1[v]);
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) {
-                    acc[v][e] = fmaf(a0, to_f32(e0[e]), acc[v][e]);
-                    acc[v][e] = fmaf(a1, to_f32(e1[e]), acc[v][e]);
-                }
-            }
+            fma_vectors<WT, V, NP>(acc, a0, q0, active);
+            fma_vectors<WT, V, NP>(acc, a1, q1, active);
         }
         if (t < n) {
             const int i0 = __shfl_sync(0xffffffffu, my_idx, t);
             const float a0 = __shfl_sync(0xffffffffu, my_val, t);
             const WT *r0 = W + (int64_t)i0 * ldw + d0 + lane * EPV;
+            uint4 q0[V];
 #pragma unroll
-            for (int v = 0; v < V; ++v) {
-                if (!active[v]) continue;
-                const uint4 q = ld_w_v4(r0 + v * 32 * EPV, wpol);
-                const WT *e0 = reinterpret_cast<const WT *>(&q);
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) acc[v][e] = fmaf(a0, to_f32(e0[e]), acc[v][e]);
-            }
+            for (int v = 0; v < V; ++v) q0[v] = active[v] ? ld_w_v4(r0 + v * 32 * EPV, wpol) : make_uint4(0, 0, 0, 0);
+            fma_vectors<WT, V, NP>(acc, a0, q0, active);
         }
     }
     if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(err, kErrIndex);
@@ -348,7 +387,8 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
         float r[EPV];
 #pragma unroll
         for (int e = 0; e < EPV; ++e)
-            r[e] = acc[v][e] + (b_dec ? load_as_f32(b_dec, b_dtype, (d + e) * b_stride) : 0.f);
+            r[e] = ((e & 1) ? acc[v][e / 2].y : acc[v][e / 2].x) +
+                   (b_dec ? load_as_f32(b_dec, b_dtype, (d + e) * b_stride) : 0.f);
         OT *dst = out + row * ldo + d;
         if (out_vec && sizeof(OT) * EPV >= 8) {
             if (sizeof(OT) == sizeof(WT)) {

@@ -112,18 +112,24 @@ def _streams(dev):
 
 
 def _chunk_plan(M, C):
-    """Row counts of forward_host's chunks: a ramp of C/4 and C/2 at both ends around full
-    chunks of at most C, so the first host-to-device copy and the last device-to-host copy,
-    which nothing overlaps, move a quarter chunk each."""
+    """Row counts of forward_host's chunks. Chunk i+1's host-to-device copy runs while chunk
+    i computes, and chunk i's device-to-host copy while chunk i+1 computes; compute per row
+    is ~2.6x a copy per row (d_in=2304 over PCIe), so a copy hides behind a neighbour of
+    at least half its size. The plan therefore starts and ends with C/16 rows (the copies
+    that nothing overlaps), doubles towards the middle up to C, and splits the middle into
+    equal chunks of at most twice the ramp's last step."""
     if M <= C:
         return [M]
-    ramp = [max(1, C // 4), max(1, C // 2)]
-    mid = M - 2 * sum(ramp)
-    if mid <= 0:
-        n = -(-M // C)
-        return [M // n + (1 if i < M % n else 0) for i in range(n)]
-    n = -(-mid // C)
-    return ramp + [mid // n + (1 if i < mid % n else 0) for i in range(n)] + ramp[::-1]
+    head = []
+    n = max(1, C // 16)
+    rem = M
+    while n < C and rem >= 3 * n:
+        head.append(n)
+        rem -= 2 * n
+        n = min(C, 2 * n)
+    cap = min(C, 2 * head[-1]) if head else C
+    k = -(-rem // cap)
+    return head + [rem // k + (1 if i < rem % k else 0) for i in range(k)] + head[::-1]
 
 
 def forward_host(sae, x, out=None, *, chunk_tokens=8192):
@@ -131,8 +137,8 @@ def forward_host(sae, x, out=None, *, chunk_tokens=8192):
 
     x: [M, d_in] CPU tensor (pinned for the copies to overlap; pageable x is pinned first).
     out: optional [M, d_in] pinned CPU tensor of W_dec's dtype to write into.
-    The batch runs in chunks of at most `chunk_tokens` rows on sae's device (quarter and half
-    chunks at both ends): chunk i+1's host-to-device copy and chunk i-1's device-to-host copy
+    The batch runs in chunks of at most `chunk_tokens` rows on sae's device (halving towards
+    both ends, down to a sixteenth): chunk i+1's host-to-device copy and chunk i-1's device-to-host copy
     run on their own streams while chunk i is encoded and decoded on the current stream, with
     two device buffers per direction. One host sync at
     the end waits for the last copy and reads every chunk's overflow flag; a chunk whose CSR

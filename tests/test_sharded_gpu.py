@@ -29,6 +29,7 @@ def make_sae(device):
     """A sparse bf16 JumpReLU SAE (L0 ~ 70) and a token batch, the same in every process."""
     import oracle
 
+    torch.manual_seed(0)  # the constructor draws W_dec from the global generator: same SAE in every process
     g = torch.Generator().manual_seed(0)
     sae = oracle.RefSAE(D_IN, D_SAE, "jumprelu")
     sae.b_enc.copy_(torch.randn(D_SAE, generator=g) * 0.1)
