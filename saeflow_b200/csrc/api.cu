@@ -252,6 +252,7 @@ struct EncodePlan {
     bool b_mn;
     int64_t w_pitch; // pitch of W_enc as TMA sees it (elements)
     size_t xs_bytes, wp_bytes;
+    bool fused_x;    // the CTA-pair kernel's converter warps read x itself and shift it (no copy)
 };
 
 int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int variant, EncodePlan *pl) {
@@ -278,6 +279,13 @@ int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int vari
     // Shifted x: rows padded to 16 B (vector kernel writes 8 elements per item).
     pl->a_pitch = round_up(K > 0 ? K : 1, 8);
     pl->xs_bytes = (size_t)(M * pl->a_pitch * es);
+    // Fused shift: 16-bit operands on the CTA-pair kernel (M > 128 rows) with x in W_enc's
+    // dtype, K-contiguous, 16-byte-aligned rows and d_in a multiple of 8 (whole 16-byte
+    // chunks). Otherwise the shift pass writes the shifted copy the kernel reads.
+    pl->fused_x = kFusedShift && tc && wdt != SF_F32 && M > 128 && variant != SF_VARIANT_TCGEN05_SINGLE &&
+                  x->dtype == wdt && x->stride_col == 1 && (x->stride_row % 8) == 0 && x->stride_row >= K &&
+                  aligned16(x->data) && (K % 8) == 0;
+    if (pl->fused_x) pl->xs_bytes = 0;
     pl->wp_bytes = 0;
     pl->w_direct = true;
     pl->b_mn = true;
@@ -311,6 +319,27 @@ int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int vari
 }
 
 size_t plan_workspace(const EncodePlan &pl) { return round_up((int64_t)pl.xs_bytes, 256) + pl.wp_bytes; }
+
+// The GEMM's A operand: x itself with b_dec for the converter warps (fused shift), or the
+// shifted copy `xs` that run_shift_convert wrote.
+void set_a_operand(GemmOperands &g, const EncodePlan &pl, const sf_matrix *x, const sf_vector *b_dec, void *xs) {
+    g.bdec = nullptr;
+    g.bdec_mode = 0;
+    if (!pl.fused_x) {
+        g.a = xs;
+        g.a_pitch = pl.a_pitch;
+        return;
+    }
+    g.a = x->data;
+    g.a_pitch = x->stride_row;
+    if (b_dec && b_dec->data) {
+        g.bdec = b_dec->data;
+        g.bdec_dtype = b_dec->dtype;
+        g.bdec_stride = b_dec->stride;
+        const bool packed = b_dec->stride == 1 && aligned16(b_dec->data);
+        g.bdec_mode = !packed ? 3 : (b_dec->dtype == SF_F32 ? 2 : 1);
+    }
+}
 
 int run_shift_convert(const sf_matrix *x, const sf_vector *b_dec, int mdt, void *xs, int64_t pitch, cudaStream_t s) {
     const int64_t M = x->rows, K = x->cols;
@@ -437,8 +466,10 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     void *xs = ws;
     void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
-    st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
-    if (st) return st;
+    if (!pl.fused_x) {
+        st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
+        if (st) return st;
+    }
 
     EpilogueArgs ep{};
     ep.b_enc = b_enc->data;
@@ -465,8 +496,7 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
                                W_enc->stride_row, W_enc->stride_col, M, N, K, ep, s);
 
     GemmOperands g{};
-    g.a = xs;
-    g.a_pitch = pl.a_pitch;
+    set_a_operand(g, pl, x, b_dec, xs);
     g.ab_fmt = pl.ab_fmt;
     g.M = M;
     g.N = N;
@@ -521,11 +551,12 @@ int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vec
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     void *xs = ws;
     void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
-    st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
-    if (st) return st;
+    if (!pl.fused_x) {
+        st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
+        if (st) return st;
+    }
     GemmOperands g{};
-    g.a = xs;
-    g.a_pitch = pl.a_pitch;
+    set_a_operand(g, pl, x, b_dec, xs);
     g.ab_fmt = pl.ab_fmt;
     g.M = M;
     g.N = N;
@@ -760,11 +791,12 @@ int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *
     void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
     auto *cand = reinterpret_cast<unsigned long long *>(ws + cand_off);
 
-    st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
-    if (st) return st;
+    if (!pl.fused_x) {
+        st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
+        if (st) return st;
+    }
     GemmOperands g{};
-    g.a = xs;
-    g.a_pitch = pl.a_pitch;
+    set_a_operand(g, pl, x, b_dec, xs);
     g.ab_fmt = pl.ab_fmt;
     g.M = M;
     g.N = N;

@@ -31,6 +31,7 @@
 // shared memory would compete with the tensor cores for shared-memory bandwidth.
 #include <algorithm>
 #include <cstddef>
+#include <cstring>
 #include <mutex>
 
 #include <cudaTypedefs.h>
@@ -94,6 +95,13 @@ struct TcParams {
     void *stage_val;           // [stage_cap] values in out_dtype
     unsigned *csr_state;       // [0] staging cursor, [1] overflow flag
     unsigned stage_cap;
+    // A operand of the converter warps (see GemmOperands)
+    const void *xa;
+    int64_t xa_pitch;
+    const void *bdec;
+    int bdec_dtype;
+    int64_t bdec_stride;
+    int bdec_mode;
 };
 
 // The staged bias / cut arrays are read as float4: they must start on 16-byte boundaries.
@@ -550,6 +558,71 @@ __device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared 
     }
 }
 
+// ------------------------------------------------------------------ fused shift (A converter)
+// The 16-bit CTA-pair kernel builds its A tiles itself: four converter warps per CTA read
+// 16-byte chunks of x rows from global memory (L2), compute (x - b_dec) in fp32 and round it
+// to the MMA dtype (the reference prologue, saeflow/kernels/encode.py:72), and store the
+// chunks in the 128-byte-swizzled layout the MMA descriptors expect. This takes the place
+// of both the separate shift pass over x (a read and a write of x in HBM) and the TMA load
+// of the shifted copy; shared-memory traffic is unchanged (the converters write what the
+// TMA wrote).
+constexpr int kConvThreads = 128;
+
+// -b_dec[k0 .. k0+8) in fp32 pairs (zeros without a shift or past K).
+__device__ __forceinline__ void neg_bdec_chunk(const TcParams &p, int k0, float2 (&nb)[4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) nb[i] = make_float2(0.f, 0.f);
+    if (p.bdec_mode == 0 || k0 >= p.K) return;
+    if (p.bdec_mode == 1) {
+        const uint4 q = __ldg(reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.bdec) + k0));
+        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float2 f;
+            if (p.bdec_dtype == SF_BF16) {
+                f = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u));
+            } else {
+                __half2 h;
+                memcpy(&h, &w[i], 4);
+                f = __half22float2(h);
+            }
+            nb[i] = make_float2(-f.x, -f.y);
+        }
+    } else if (p.bdec_mode == 2) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(static_cast<const float *>(p.bdec) + k0);
+        const float4 a = __ldg(b4), b = __ldg(b4 + 1);
+        nb[0] = make_float2(-a.x, -a.y), nb[1] = make_float2(-a.z, -a.w);
+        nb[2] = make_float2(-b.x, -b.y), nb[3] = make_float2(-b.z, -b.w);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            nb[i] = make_float2(-load_as_f32(p.bdec, p.bdec_dtype, (int64_t)(k0 + 2 * i) * p.bdec_stride),
+                                -load_as_f32(p.bdec, p.bdec_dtype, (int64_t)(k0 + 2 * i + 1) * p.bdec_stride));
+    }
+}
+
+// Eight 16-bit elements of x plus -b_dec in fp32, rounded to nearest in the same 16-bit type.
+template <int AB_FMT>
+__device__ __forceinline__ uint4 shift_chunk(uint4 v, const float2 (&nb)[4]) {
+    uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (AB_FMT == 1) {
+            const float2 f = __fadd2_rn(make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u)),
+                                        nb[i]);
+            const __nv_bfloat162 r = __float22bfloat162_rn(f);
+            memcpy(&w[i], &r, 4);
+        } else {
+            __half2 h;
+            memcpy(&h, &w[i], 4);
+            const float2 f = __fadd2_rn(__half22float2(h), nb[i]);
+            const __half2 r = __float22half2_rn(f);
+            memcpy(&w[i], &r, 4);
+        }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <int AB_FMT, bool B_MN, int MODE, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     encode_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -756,7 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // -------------------------------------------------------------------------------------
 // CTA-pair kernel (cluster of 2, tcgen05 cta_group::2): 256 x 256 tile per pair.
 template <int AB_FMT, bool B_MN, int MODE, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kConvThreads : kThreads, 1)
     encode_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const TcParams p) {
     constexpr int ES = (AB_FMT == 2) ? 4 : 2;
@@ -768,7 +841,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int HALF_N = kBN / 2;            // columns of W_enc this CTA holds per stage
     constexpr int A_BYTES = 128 * 128;         // 128 rows x 128 B
     constexpr int B_BYTES = HALF_N * 128;      // 128 columns x 128 B
-    constexpr uint32_t PAIR_TX = 2u * (A_BYTES + B_BYTES);
+    constexpr bool CONV_A = AB_FMT != 2 && kFusedShift;  // A tiles from the converter warps
+    constexpr uint32_t PAIR_TX = CONV_A ? 2u * B_BYTES : 2u * (A_BYTES + B_BYTES);
     constexpr uint32_t IDESC = make_idesc(AB_FMT, B_MN, 256, kBN);
 
     extern __shared__ uint8_t smem_raw[];
@@ -787,7 +861,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&sh->full[s], 1);   // leader's: its expect_tx arrive + both CTAs' bytes
+            // leader's: its expect_tx arrive + both CTAs' TMA bytes (+ one arrive per
+            // converter warp of both CTAs when the converters build A)
+            mbar_init(&sh->full[s], CONV_A ? 1 + 2 * kConvThreads / 32 : 1);
             mbar_init(&sh->empty[s], 1);  // one commit from the leader's MMA thread
         }
         for (int b = 0; b < 2; ++b) {
@@ -816,6 +892,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_remote_u32(peer_abort, 1u);
         return false;
     };
+    // The same with cluster-scope acquire: for phases completed by the peer CTA's converter
+    // warps, whose shared-memory writes the MMAs read.
+    auto wait_cluster = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (mbar_wait_cluster(bar, parity, abort_flag, p.err)) return true;
+        st_remote_u32(peer_abort, 1u);
+        return false;
+    };
 
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer (both CTAs)
@@ -841,8 +924,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                             armed |= 1u << stage;
                             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
                         }
-                        tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_leader, kb * BK,
-                                         un.m_blk * 256 + (int)rank * 128, pol_x);
+                        if (!CONV_A)
+                            tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_leader, kb * BK,
+                                             un.m_blk * 256 + (int)rank * 128, pol_x);
                         uint8_t *b_dst = sB + stage * B_BYTES;
                         const int n0 = n_blk * kBN + (int)rank * HALF_N;
                         if (B_MN) {
@@ -890,7 +974,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + acc * kAccCols;
                     for (int kb = 0; kb < p.num_kb; ++kb) {
-                        if (!wait(&sh->full[stage], phase)) {
+                        if (!(CONV_A ? wait_cluster(&sh->full[stage], phase) : wait(&sh->full[stage], phase))) {
                             ok = false;
                             break;
                         }
@@ -929,7 +1013,75 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_commit_pair(map_to_rank(smem_u32(&sh->drain), 0));
             mbar_wait_drain(&sh->drain, 0, p.err);
         }
-    } else {
+    } else if (CONV_A && warp >= 6) {
+        // ---------------------------------------------------------------- A converters (both CTAs)
+        // Thread ct owns 16-byte chunk c = ct % 8 of the 128-byte K row of rows
+        // ct / 8 + 16 i (i < 8) of this CTA's 128 rows, every stage. Stage j+1's loads are in
+        // flight while stage j is converted and stored.
+        const int ct = threadIdx.x - kThreads;
+        const int c = ct & 7;
+        const int r0 = ct >> 3;
+        const uint32_t swz = (uint32_t)(((c ^ (r0 & 7)) << 4) + r0 * 128);  // r & 7 == r0 & 7 for every row
+        const uint16_t *xa = static_cast<const uint16_t *>(p.xa);
+        int u = pair, nt = 0, kb = 0;
+        Unit un{};
+        bool have = u < p.num_units;
+        if (have) un = unit_coords(p, u, MODE);
+        auto load = [&](uint4 (&v)[8], float2 (&nb)[4]) {
+            const int k0 = kb * 64 + c * 8;
+            const int64_t row_base = (int64_t)un.m_blk * 256 + (int)rank * 128 + r0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int64_t row = row_base + 16 * i;
+                v[i] = (row < p.M && k0 < p.K)
+                           ? __ldg(reinterpret_cast<const uint4 *>(xa + row * p.xa_pitch + k0))
+                           : make_uint4(0u, 0u, 0u, 0u);
+            }
+            neg_bdec_chunk(p, k0, nb);
+        };
+        auto advance = [&]() {
+            if (++kb < p.num_kb) return;
+            kb = 0;
+            if (++nt < un.n_count) return;
+            nt = 0;
+            u += npairs;
+            have = u < p.num_units;
+            if (have) un = unit_coords(p, u, MODE);
+        };
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        uint4 va[8], vb[8];
+        float2 na[4], nb[4];
+        auto put = [&](const uint4 (&v)[8], const float2 (&n)[4]) -> bool {
+            if (!wait(&sh->empty[stage], phase ^ 1u)) return false;
+            uint8_t *dst = sA + stage * A_BYTES + swz;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                *reinterpret_cast<uint4 *>(dst + i * 16 * 128) = shift_chunk<AB_FMT>(v[i], n);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(map_to_rank(smem_u32(&sh->full[stage]), 0));
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+            }
+            return true;
+        };
+        if (have) load(va, na);
+        while (ok && have) {
+            advance();
+            const bool next = have;
+            if (next) load(vb, nb);
+            ok = put(va, na);
+            if (!ok || !next) break;
+            advance();
+            const bool next2 = have;
+            if (next2) load(va, na);
+            ok = put(vb, nb);
+            if (!next2) break;
+        }
+    } else if (warp < 6) {
         // ---------------------------------------------------------------- epilogue (both CTAs)
         const int et = threadIdx.x - 64;
         const int quad = warp & 3;
@@ -1038,6 +1190,7 @@ template <int AB_FMT, bool B_MN, int MODE, int STAGES>
 int launch_pair(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
                 cudaStream_t stream) {
     auto kern = encode_tc2_kernel<AB_FMT, B_MN, MODE, STAGES>;
+    constexpr int threads = (AB_FMT != 2 && kFusedShift) ? kThreads + kConvThreads : kThreads;
     const size_t smem = 1024 + (size_t)STAGES * (kBM * 128 + (kBN / 2) * 128) + sizeof(TcShared) + extra_smem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(encode_tc2)");
@@ -1047,7 +1200,7 @@ int launch_pair(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
@@ -1096,6 +1249,12 @@ void fill_common(TcParams &p, const GemmOperands &g, bool pair, unsigned *err) {
     p.num_n_tiles = (int)((g.N + kBN - 1) / kBN);
     p.num_kb = (int)((g.K + (128 / es) - 1) / (128 / es));
     p.err = err;
+    p.xa = g.a;
+    p.xa_pitch = g.a_pitch;
+    p.bdec = g.bdec;
+    p.bdec_dtype = g.bdec_dtype;
+    p.bdec_stride = g.bdec_stride;
+    p.bdec_mode = g.bdec ? g.bdec_mode : 0;
 }
 
 }  // namespace
@@ -1197,6 +1356,11 @@ int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &
 // CTAs (or CTA pairs) in whole waves to within kTopkWaveEff; failing that, the best-balanced
 // count up to 32.
 constexpr double kTopkWaveEff = 0.94;
+// Smallest per-row candidate buffer (entries) the top-k kernel's operand ring may leave room
+// for; a smaller buffer buys operand stages at the price of more frequent merges.
+#ifndef SF_TOPK_MIN_BUF
+#define SF_TOPK_MIN_BUF 48
+#endif
 int topk_chunks(int64_t M, int64_t N) {
     const bool pair = M > kBM;
     const int bm = pair ? 256 : kBM;
@@ -1256,17 +1420,20 @@ int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t strea
                           (long)(tk.k * row_entry);
         return std::min<long>(64, left / (long)row_entry);
     };
-    int stages = pair ? 4 : 3;
-    while (stages > 2 && buffer_for(stages) < 48) --stages;
+    int stages = pair ? 6 : 4;
+    while (stages > 2 && buffer_for(stages) < SF_TOPK_MIN_BUF) --stages;
     if (buffer_for(stages) < kTopkGroup)
         return set_error(SF_ERR_UNSUPPORTED, "top-k k=%d does not fit in shared memory", tk.k);
     p.topk_buf = (int)buffer_for(stages);
     const size_t extra = (size_t)(tk.k + p.topk_buf) * row_entry;
     if (pair) {
+        if (stages == 6) return dispatch<kTopk, 6, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
+        if (stages == 5) return dispatch<kTopk, 5, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
         if (stages == 4) return dispatch<kTopk, 4, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
         if (stages == 3) return dispatch<kTopk, 3, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
         return dispatch<kTopk, 2, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
     }
+    if (stages == 4) return dispatch<kTopk, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
     if (stages == 3) return dispatch<kTopk, 3, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
     return dispatch<kTopk, 2, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, extra, stream);
 }

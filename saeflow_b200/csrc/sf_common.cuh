@@ -130,6 +130,43 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
 }
 
+// mbar_try_wait with cluster-scope acquire: pairs with arrivals made by another CTA of the
+// cluster with release semantics at cluster scope (mbar_arrive_remote).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar_addr, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred P;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, P;\n\t}"
+        : "=r"(ok)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait with cluster-scope acquire (same limits and abort behaviour).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                                  unsigned *err_word) {
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    const unsigned long long t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(a, parity)) return true;
+        if (*abort_flag) return false;
+        if ((i & 31u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(err_word, kErrTimeout);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy reads
+// of them (tcgen05.mma operands written by threads rather than by TMA).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Bounded wait that ignores the abort flag: used only to let copies in flight land before
 // a kernel that gave up exits.
 __device__ __forceinline__ void mbar_wait_drain(uint64_t *bar, uint32_t parity, unsigned *err_word) {

@@ -19,7 +19,24 @@ struct GemmOperands {
     bool b_mn_major;
     int ab_fmt;  // 0 fp16, 1 bf16, 2 tf32 (fp32 storage)
     int64_t M, N, K;
+    // Fused shift (16-bit CTA-pair kernel, kFusedShift): the kernel's converter warps read A
+    // rows from `a` (K-contiguous, pitch a_pitch elements, 16-byte aligned, K % 8 == 0) and
+    // subtract `bdec` in fp32 before rounding to the MMA dtype. bdec_mode: 0 no shift (the
+    // rows are already shifted), 1 contiguous 16-byte-aligned 16-bit, 2 contiguous
+    // 16-byte-aligned fp32, 3 any dtype and stride.
+    const void *bdec;
+    int bdec_dtype;
+    int64_t bdec_stride;
+    int bdec_mode;
 };
+
+// The CTA-pair kernel for 16-bit operands builds its A tiles with converter warps from x
+// itself, subtracting b_dec on the way (no shifted copy of x in HBM). 0 restores the
+// separate shift pre-pass and TMA loads of the shifted copy.
+#ifndef SF_FUSED_SHIFT
+#define SF_FUSED_SHIFT 1
+#endif
+constexpr bool kFusedShift = SF_FUSED_SHIFT != 0;
 
 struct EpilogueArgs {
     const void *b_enc;

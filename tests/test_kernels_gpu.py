@@ -116,6 +116,45 @@ def test_cta_pair_kernel_matches_single_cta_kernel(dtype, shape, colmajor):
     torch.testing.assert_close(outs[0], outs[1], atol=TOL[dtype], rtol=TOL[dtype])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("bdec_kind", ["none", "same", "fp32", "strided"])
+@pytest.mark.parametrize("route", ["dense", "csr", "topk"])
+def test_pair_kernel_fused_shift_matches_shifted_copy(dtype, bdec_kind, route):
+    """The CTA-pair kernel's converter warps shift x on the fly (x contiguous, in W_enc's
+    dtype) or copy a pre-shifted x (x at an address TMA-style loads cannot start from, or
+    fp32 x): both give the same bits, for b_dec absent, in x's dtype, in fp32 and strided,
+    on the dense, CSR-staging and top-k epilogues, and match the oracle."""
+    M, d_in, d_sae = 300, 264, 1000  # M > 128: the pair kernel; d_in % 64 != 0: a partial K block
+    sae = make_sae(d_in, d_sae, "jumprelu", dtype).to("cuda")
+    x = torch.randn(M, d_in, device="cuda").to(dtype)
+    b = {"none": None, "same": sae.b_dec, "fp32": sae.b_dec.float(),
+         "strided": torch.stack([sae.b_dec, -sae.b_dec], 1)[:, 0]}[bdec_kind]
+    x_odd = torch.zeros(M, d_in + 1, device="cuda", dtype=dtype)[:, 1:]  # 2-byte offset: shifted-copy path
+    x_odd.copy_(x)
+    x32 = x.float()  # fp32 x with 16-bit W_enc: shifted-copy path
+    b_ref = b if b is not None else torch.zeros(d_in, device="cuda", dtype=dtype)
+
+    def run(xx):
+        if route == "dense":
+            rn = torch.zeros(M, device="cuda", dtype=torch.int32)
+            return [fused_encode(xx, sae.W_enc, sae.b_enc, b, sae.threshold, "jumprelu", row_nnz=rn,
+                                 out_dtype=dtype), rn]
+        if route == "csr":
+            return list(encode_csr(xx, sae.W_enc, sae.b_enc, b, sae.threshold, "jumprelu"))
+        return list(topk_encode(xx, sae.W_enc, sae.b_enc, b_ref, 16))
+
+    want = run(x)
+    # fp32 x stores CSR / top-k values in fp32, so it is compared on the dense route only
+    for other in ((x_odd, x32) if route == "dense" else (x_odd,)):
+        got = run(other)
+        for u, v in zip(got, want):
+            assert u.dtype == v.dtype and u.shape == v.shape
+            bits = (lambda t: t.view(torch.int16)) if v.dtype in (torch.bfloat16, torch.float16) else (lambda t: t)
+            assert torch.equal(bits(u), bits(v))
+    if route == "dense":
+        check_encode(want[0], x, sae.W_enc, sae.b_enc, b_ref, sae.threshold, "jumprelu", want[1])
+
+
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_fused_encode_out_dtype(out_dtype):
     sae = make_sae(96, 300, "relu", torch.bfloat16).to("cuda")
