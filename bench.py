@@ -332,9 +332,9 @@ def run_ours(args, rank, world, device):
             for name in ("W_enc", "b_enc", "W_dec", "b_dec"):
                 getattr(sae, name).grad = None
             return out
-        # forward 4 (3 for TopK; the b_dec shift is fused into the encoder); backward: count, scan, scatter, 2 in-column sorts, 2 x (gather, carry),
+        # forward 5 (4 for TopK); backward: count, scan, scatter, 2 in-column sorts, 2 x (gather, carry),
         # transpose of dW_enc, matvec for db_dec (x takes no gradient here)
-        launches_per_step = 15
+        launches_per_step = 16
     elif sharded is not None:
         n_chunks = (T + args.chunk_tokens - 1) // args.chunk_tokens
 
@@ -343,8 +343,7 @@ def run_ours(args, rank, world, device):
             out = sharded.forward(x)
             ev[3].record(stream)
             return out
-        # per token chunk: encode+stage (b_dec shift fused), indptr scan, place, decode
-        launches_per_step = 4 * n_chunks
+        launches_per_step = 5 * n_chunks  # per token chunk: shift, encode+stage, indptr scan, place, decode
     elif cfg_id == 3:
         csr = make_csr(cfg_id, rank, device, T)
 
@@ -366,7 +365,7 @@ def run_ours(args, rank, world, device):
             out = sparse_decode(indptr, idx.view(-1), vals.view(-1), sae.W_dec, sae.b_dec)
             ev[3].record(stream)
             return out
-        launches_per_step = 3  # encode+top-k (b_dec shift fused), merge, decode
+        launches_per_step = 4  # shift, encode+top-k, merge, decode
     elif args.route == "dense" or cfg_id == 1:
         # The reference's route: dense features, then compaction (IEEE fp32 always takes it).
         x = make_tokens(cfg_id, rank, device, T)
@@ -384,9 +383,7 @@ def run_ours(args, rank, world, device):
             step.nnz = csr[1].numel()
             del f
             return out
-        # shift pass (the fp32 CUDA-core encoder has no fused shift; bf16 shifts in the
-        # encoder), encode, indptr scan, compact, decode
-        launches_per_step = 5 if cfg_id == 1 else 4
+        launches_per_step = 5  # shift, encode, indptr scan, compact, decode
     else:
         # Encode straight to CSR (what saeflow_b200.encode_sparse runs): no dense features.
         if cfg_id != 5:
@@ -413,7 +410,7 @@ def run_ours(args, rank, world, device):
                 step.checks.append((indptr[-1], overflow))
             return out_buf
         step.checks = []
-        launches_per_step = 4 * quads  # per chunk: encode+stage (b_dec shift fused), indptr scan, place, decode
+        launches_per_step = 5 * quads  # per chunk: shift, encode+stage, indptr scan, place, decode
 
     def barrier():
         if world > 1:

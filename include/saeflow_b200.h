@@ -94,12 +94,9 @@ SF_API int sf_abi_version(void);
 SF_API int sf_device_error(uint32_t *code);
 
 /*
- * Workspace bytes sf_fused_encode needs for these operands: the b_dec-shifted,
- * dtype-converted copy of x when the encoder cannot shift x on the fly (x not in W_enc's
- * 16-bit dtype, not K-contiguous with 16-byte-aligned rows, d_in not a multiple of 8, at
- * most 128 rows, or fp32 W_enc), plus a repacked W_enc when its layout cannot be read by
- * TMA; 0 for the common case. Replaces the allocation-free Triton launch of
- * saeflow/kernels/encode.py:115-139.
+ * Workspace bytes sf_fused_encode needs for these operands (the b_dec-shifted,
+ * dtype-converted copy of x, plus a repacked W_enc when its layout cannot be read by
+ * TMA). Replaces the allocation-free Triton launch of saeflow/kernels/encode.py:115-139.
  */
 SF_API int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int allow_tf32,
                               int variant, size_t *bytes);
@@ -208,11 +205,8 @@ SF_API int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *ind
  *
  * The workspace is a 16 MiB array in the library's device image (held by every GPU that
  * loads the library's device code, until exit); this call allocates nothing. Operands
- * whose sf_fused_encode_workspace exceeds 16 MiB are rejected with SF_ERR_WORKSPACE. The
- * workspace holds a shifted copy of x only when the encoder cannot read x in place (x not
- * in W_enc's dtype, not K-contiguous with 16-byte-aligned rows, d_in not a multiple of 8, or
- * at most 128 rows); e.g. fp32 x with bf16 W_enc and d_in=2304: at most 3640 rows per
- * call. W_enc must be readable in
+ * whose sf_fused_encode_workspace exceeds 16 MiB are rejected with SF_ERR_WORKSPACE
+ * (e.g. bf16 x with d_in=2304: at most 3640 rows per call). W_enc must be readable in
  * place: a 16-bit W_enc contiguous along one dimension with a 16-byte-aligned base and
  * row pitch, or on the TF32 path an fp32 W_enc in column-major layout (or the IEEE fp32
  * path, which never copies W_enc); other layouts need a repacked copy of W_enc that the

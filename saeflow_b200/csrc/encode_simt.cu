@@ -2,18 +2,14 @@
 //
 // The reference computes fp32 inputs with `input_precision="ieee"` unless TF32 is
 // allowed (saeflow/kernels/encode.py:118-120); this kernel is that path. Epilogue
-// semantics are identical to the tensor-core kernel (encode.py:77-91).
+// semantics are identical to the tensor-core kernel (encode.py:195-208).
 //
 // 128 x (64*NF) output tile per CTA, K in steps of 8 through double-buffered shared memory,
 // 256 threads each owning an 8 x (4*NF) register block (rows {4ty..4ty+3, 64+4ty..}, columns
-// {64q+4tx..64q+4tx+3 : q < NF}). The products run as sm_100 packed fp32 FMAs
-// (__ffma2_rn: two IEEE round-to-nearest FMAs per instruction, each lane bit-identical to
-// fmaf): accumulator pairs hold two adjacent columns of one row, W_enc supplies the column
-// pair as it lies in shared memory, and x is staged in shared memory with every value
-// written twice, so a 16-byte load yields two ready (x, x) pairs and no register shuffling
-// is needed. Per K step a thread issues 4 + NF shared loads and 16*NF packed FMAs (the
-// scalar version needed 2 + NF loads and 32*NF FMAs and was instruction-issue bound with
-// the FMA pipe 62% busy). NF=4 (128 x 256 tiles) is the default; NF=2 serves d_sae < 256.
+// {64q+4tx..64q+4tx+3 : q < NF}) so the shared-memory reads are conflict-free float4
+// broadcasts. NF=4 (128 x 256 tiles, 128 accumulators per thread) is the default: per K step
+// a thread issues 6 shared loads for 128 FMAs (4 for 64 with NF=2), which moved the FMA pipe
+// from 62% busy (instruction-issue bound) toward its peak; NF=2 serves d_sae < 256.
 #include "sf_common.cuh"
 #include "sf_internal.h"
 
@@ -45,12 +41,12 @@ __device__ __forceinline__ void simt_store4(void *out, int64_t sm, int64_t sn, i
 }
 
 template <int NF>
-__global__ void __launch_bounds__(SB_T, 1)
+__global__ void __launch_bounds__(SB_T, NF == 2 ? 2 : 1)
     encode_simt_kernel(const float *__restrict__ xs, int64_t ldx, const float *__restrict__ W, int64_t swk,
                        int64_t swn, int M, int N, int K, EpilogueArgs ep, int w_vec) {
     constexpr int SB_N = 64 * NF;
     constexpr int BQ = NF / 2;  // float4 loads of the B tile per thread per K step
-    __shared__ __align__(16) float2 As[2][SB_K][SB_M];  // (x, x): each value twice
+    __shared__ __align__(16) float As[2][SB_K][SB_M + 4];
     __shared__ __align__(16) float Bs[2][SB_K][SB_N + 4];
     __shared__ float s_bias[SB_N], s_thr[SB_N];
 
@@ -93,22 +89,21 @@ __global__ void __launch_bounds__(SB_T, 1)
         }
     };
     auto store_tile = [&](int buf) {
-        As[buf][a_kq + 0][a_row] = make_float2(ra.x, ra.x);
-        As[buf][a_kq + 1][a_row] = make_float2(ra.y, ra.y);
-        As[buf][a_kq + 2][a_row] = make_float2(ra.z, ra.z);
-        As[buf][a_kq + 3][a_row] = make_float2(ra.w, ra.w);
+        As[buf][a_kq + 0][a_row] = ra.x;
+        As[buf][a_kq + 1][a_row] = ra.y;
+        As[buf][a_kq + 2][a_row] = ra.z;
+        As[buf][a_kq + 3][a_row] = ra.w;
 #pragma unroll
         for (int q = 0; q < BQ; ++q)
             *reinterpret_cast<float4 *>(&Bs[buf][b_k][b_nq + q * 128]) =
                 make_float4(rb[q][0], rb[q][1], rb[q][2], rb[q][3]);
     };
 
-    // acc[i][2h + c]: row i of the thread's block, columns 64h + 4tx + 2c and + 2c + 1.
-    float2 acc[8][2 * NF];
+    float acc[8][4 * NF];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 2 * NF; ++j) acc[i][j] = make_float2(0.f, 0.f);
+        for (int j = 0; j < 4 * NF; ++j) acc[i][j] = 0.f;
 
     const int nk = (K + SB_K - 1) / SB_K;
     load_tile(0);
@@ -119,28 +114,19 @@ __global__ void __launch_bounds__(SB_T, 1)
         if (kt + 1 < nk) load_tile((kt + 1) * SB_K);
 #pragma unroll
         for (int kk = 0; kk < SB_K; ++kk) {
-            float2 a[8];
-            {
-                const float4 p0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
-                const float4 p1 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4 + 2]);
-                const float4 p2 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);
-                const float4 p3 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4 + 2]);
-                a[0] = make_float2(p0.x, p0.y), a[1] = make_float2(p0.z, p0.w);
-                a[2] = make_float2(p1.x, p1.y), a[3] = make_float2(p1.z, p1.w);
-                a[4] = make_float2(p2.x, p2.y), a[5] = make_float2(p2.z, p2.w);
-                a[6] = make_float2(p3.x, p3.y), a[7] = make_float2(p3.z, p3.w);
-            }
-            float2 b[2 * NF];
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float b[4 * NF];
 #pragma unroll
             for (int q = 0; q < NF; ++q) {
                 const float4 bq = *reinterpret_cast<const float4 *>(&Bs[buf][kk][q * 64 + tx * 4]);
-                b[2 * q] = make_float2(bq.x, bq.y);
-                b[2 * q + 1] = make_float2(bq.z, bq.w);
+                b[4 * q + 0] = bq.x, b[4 * q + 1] = bq.y, b[4 * q + 2] = bq.z, b[4 * q + 3] = bq.w;
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 2 * NF; ++j) acc[i][j] = __ffma2_rn(a[i], b[j], acc[i][j]);
+                for (int j = 0; j < 4 * NF; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
         }
         if (kt + 1 < nk) store_tile(buf ^ 1);
         __syncthreads();
@@ -155,11 +141,10 @@ __global__ void __launch_bounds__(SB_T, 1)
 #pragma unroll
         for (int h = 0; h < NF; ++h) {
             const int c = h * 64 + tx * 4;
-            const float sums[4] = {acc[i][2 * h].x, acc[i][2 * h].y, acc[i][2 * h + 1].x, acc[i][2 * h + 1].y};
             float v[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float pre = sums[j] + s_bias[c + j];
+                const float pre = acc[i][h * 4 + j] + s_bias[c + j];
                 float o = fmaxf(pre, 0.f);
                 if (ep.activation == SF_ACT_JUMPRELU) o = (pre > s_thr[c + j]) ? o : 0.f;
                 o = round_to(o, ep.out_dtype);

@@ -30,11 +30,15 @@ struct GemmOperands {
     int bdec_mode;
 };
 
-// The CTA-pair kernel for 16-bit operands builds its A tiles with converter warps from x
-// itself, subtracting b_dec on the way (no shifted copy of x in HBM). 0 restores the
-// separate shift pre-pass and TMA loads of the shifted copy.
+// 1: the CTA-pair kernel for 16-bit operands builds its A tiles with converter warps that
+// read x itself and subtract b_dec on the way (no shifted copy of x in HBM, no shift pass).
+// 0 (default): a separate pass writes the shifted copy and TMA loads it. Measured on B200
+// at config 2 (16384 x 2304 -> 65536 bf16), the converter warps cannot keep enough loads
+// in flight beside the epilogue's registers (warps stalled on L2 latency, tensor pipe 19%
+// busy against 81%): encode 12.07 ms against 3.55 ms for the pass + TMA, whose shift pass
+// costs 38 us.
 #ifndef SF_FUSED_SHIFT
-#define SF_FUSED_SHIFT 1
+#define SF_FUSED_SHIFT 0
 #endif
 constexpr bool kFusedShift = SF_FUSED_SHIFT != 0;
 

@@ -51,26 +51,17 @@ def test_invalid_arguments_are_rejected_before_any_launch():
 def test_workspace_sizes():
     lib = _abi.load()
     need = ctypes.c_size_t(0)
-    # bf16 x [16384, 2304] (contiguous, aligned), W_enc row-major [2304, 65536]: the encoder
-    # shifts x on the fly, no workspace
-    x = _abi.SfMatrix(16, 1, 0, 16384, 2304, 2304, 1)
+    # bf16 x [16384, 2304], W_enc row-major [2304, 65536]: shifted x copy only, whatever x's
+    # dtype and address (fp32 x, a 2-byte-offset base)
     W = _abi.SfMatrix(16, 1, 0, 2304, 65536, 65536, 1)
-    assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
-    assert need.value == 0
-    # x it cannot read in place (fp32 x, a misaligned base, at most 128 rows, the
-    # single-CTA kernel): the shifted bf16 copy of x
-    for xs in (_abi.SfMatrix(16, 0, 0, 16384, 2304, 2304, 1), _abi.SfMatrix(18, 1, 0, 16384, 2304, 2304, 1)):
-        assert lib.sf_fused_encode_workspace(ctypes.byref(xs), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
+    for x in (_abi.SfMatrix(16, 1, 0, 16384, 2304, 2304, 1), _abi.SfMatrix(16, 0, 0, 16384, 2304, 2304, 1),
+              _abi.SfMatrix(18, 1, 0, 16384, 2304, 2304, 1)):
+        assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
         assert need.value == 16384 * 2304 * 2
-    small = _abi.SfMatrix(16, 1, 0, 128, 2304, 2304, 1)
-    assert lib.sf_fused_encode_workspace(ctypes.byref(small), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
-    assert need.value == 128 * 2304 * 2
-    assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 3, ctypes.byref(need)) == 0
-    assert need.value == 16384 * 2304 * 2
     # odd d_sae: W_enc repacked to a 16-byte row pitch
     W = _abi.SfMatrix(16, 1, 0, 2304, 129, 129, 1)
     assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
-    assert need.value == 2304 * 136 * 2
+    assert need.value == 16384 * 2304 * 2 + 2304 * 136 * 2
     # the CUDA-core kernel is fp32 only
     assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 2, ctypes.byref(need)) == \
         _abi.SF_ERR_UNSUPPORTED

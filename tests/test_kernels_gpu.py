@@ -119,11 +119,12 @@ def test_cta_pair_kernel_matches_single_cta_kernel(dtype, shape, colmajor):
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("bdec_kind", ["none", "same", "fp32", "strided"])
 @pytest.mark.parametrize("route", ["dense", "csr", "topk"])
-def test_pair_kernel_fused_shift_matches_shifted_copy(dtype, bdec_kind, route):
-    """The CTA-pair kernel's converter warps shift x on the fly (x contiguous, in W_enc's
-    dtype) or copy a pre-shifted x (x at an address TMA-style loads cannot start from, or
-    fp32 x): both give the same bits, for b_dec absent, in x's dtype, in fp32 and strided,
-    on the dense, CSR-staging and top-k epilogues, and match the oracle."""
+def test_pair_kernel_prologue_independent_of_x_layout(dtype, bdec_kind, route):
+    """The CTA-pair kernel gives the same bits for the same values of x whatever x's address
+    and dtype (contiguous, a 2-byte-offset view, fp32), for b_dec absent, in x's dtype, in
+    fp32 and strided, on the dense, CSR-staging and top-k epilogues, and matches the oracle.
+    (Builds with SF_FUSED_SHIFT=1 shift contiguous 16-bit x inside the kernel and the other
+    layouts through the shift pass, so there this compares the two prologues.)"""
     M, d_in, d_sae = 300, 264, 1000  # M > 128: the pair kernel; d_in % 64 != 0: a partial K block
     sae = make_sae(d_in, d_sae, "jumprelu", dtype).to("cuda")
     x = torch.randn(M, d_in, device="cuda").to(dtype)

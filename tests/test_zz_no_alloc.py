@@ -4,9 +4,8 @@ allocating sf_fused_encode (B200).
 The no-alloc entry point serves callers that cannot allocate device memory (a
 foreign-language host given only its input and output buffers, a process whose caching
 allocator holds the GPU's memory, a loop that cannot take cudaMalloc's synchronisation):
-its workspace is a fixed 16 MiB array in the library's device image. The workspace holds
-a shifted copy of x when x cannot be read in place (the tests use fp32 x with bf16 W_enc,
-and a column-major view of x, to make sure the scratch array is in use). This file is
+its workspace is a fixed 16 MiB array in the library's device image, which holds the
+b_dec-shifted copy of x the encoder reads. This file is
 collected last so that a run stopping at the first failure has run every other test.
 """
 
@@ -63,9 +62,9 @@ def _encode_noalloc(lib, x, W, b_enc, b_dec, thr, out, nnz):
 def test_noalloc_encode_matches_allocating_encode_on_two_calls():
     lib = _abi.load()
     K, N = 512, 4096
-    # two calls in a row, different inputs and row counts: the second must not see the
-    # first call's scratch contents. fp32 x with 16-bit W_enc (and, second, a strided view)
-    # cannot be read in place, so the shifted copy of x lives in the scratch array.
+    # two calls in a row, different inputs, row counts and x layouts (fp32 x converted to
+    # W_enc's bf16, then a column-major bf16 view): the second must not see the first
+    # call's scratch contents.
     for M, seed in ((1000, 11), (3000, 12)):
         x, W, b_enc, b_dec, thr = _operands(M, K, N, seed)
         x = x.float() if seed == 11 else x.T.contiguous().T
@@ -84,9 +83,8 @@ def test_noalloc_encode_matches_allocating_encode_on_two_calls():
 def test_noalloc_encode_rejects_operands_beyond_its_scratch():
     lib = _abi.load()
     K, N = 2304, 512
-    M = SCRATCH_BYTES // (K * 2) + 1  # one row more than the scratch's bf16 copy of x holds
+    M = SCRATCH_BYTES // (K * 2) + 1  # one row more than the scratch holds
     x, W, b_enc, b_dec, thr = _operands(M, K, N, 13)
-    x = x.float()  # fp32 x with bf16 W_enc: the shifted copy is needed
     out = torch.zeros(M, N, device="cuda", dtype=torch.bfloat16)
     nnz = torch.zeros(M, device="cuda", dtype=torch.int32)
     st = _encode_noalloc(lib, x, W, b_enc, b_dec, thr, out, nnz)
