@@ -111,25 +111,45 @@ def _streams(dev):
         return _copy_streams[dev]
 
 
-def _chunk_plan(M, C):
-    """Row counts of forward_host's chunks. Chunk i+1's host-to-device copy runs while chunk
-    i computes, and chunk i's device-to-host copy while chunk i+1 computes; compute per row
-    is ~2.6x a copy per row (d_in=2304 over PCIe), so a copy hides behind a neighbour of
-    at least half its size. The plan therefore starts and ends with C/16 rows (the copies
-    that nothing overlaps), doubles towards the middle up to C, and splits the middle into
-    equal chunks of at most twice the ramp's last step."""
+def _even_split(n, cap):
+    k = -(-n // cap)
+    return [n // k + (1 if i < n % k else 0) for i in range(k)]
+
+
+def _chunk_plan(M, C, stream=True):
+    """Row counts of forward_host's chunks (at most C each).
+
+    Only the first chunk's host-to-device copy and the last chunk's device-to-host copy are
+    exposed; compute per row is ~3x a copy per row (d_in=2304 over PCIe). stream=True (the
+    batch has device buffers of its own, so copies run ahead without waiting for a buffer):
+    C/16 rows at both ends, doubling towards the middle, which is split into equal chunks of
+    at most C and at most 2.5x the ramp's last step (a copy hides as long as each chunk is
+    at most ~2.5x the previous one).
+    stream=False (two device buffers per direction, a chunk's copy waits until the chunk
+    two before it is done): quarter and half chunks at both ends, full chunks between."""
     if M <= C:
         return [M]
-    head = []
-    n = max(1, C // 16)
-    rem = M
-    while n < C and rem >= 3 * n:
-        head.append(n)
-        rem -= 2 * n
-        n = min(C, 2 * n)
-    cap = min(C, 2 * head[-1]) if head else C
-    k = -(-rem // cap)
-    return head + [rem // k + (1 if i < rem % k else 0) for i in range(k)] + head[::-1]
+    if not stream:
+        ramp = [max(1, C // 4), max(1, C // 2)]
+        mid = M - 2 * sum(ramp)
+        if mid <= 0:
+            return _even_split(M, C)
+        return ramp + _even_split(mid, C) + ramp[::-1]
+    ramp = [n for n in (C // 16, C // 8, C // 4, C // 2) if n >= 1]
+    while ramp and M - 2 * sum(ramp) <= 0:
+        ramp.pop()
+    mid = M - 2 * sum(ramp)
+    if ramp and mid < ramp[-1]:  # fold a short middle into its two neighbours
+        mid += 2 * ramp.pop()
+    if not ramp:
+        return _even_split(M, C)
+    return ramp + _even_split(mid, min(C, max(1, int(2.5 * ramp[-1])))) + ramp[::-1]
+
+
+# Device bytes (x and x_hat together) up to which forward_host gives the whole batch device
+# buffers, so the copies stream without waiting for a buffer; larger batches cycle through
+# two chunk-sized buffers per direction.
+WHOLE_BATCH_DEVICE_BYTES = 4 << 30
 
 
 def forward_host(sae, x, out=None, *, chunk_tokens=8192):
@@ -137,12 +157,14 @@ def forward_host(sae, x, out=None, *, chunk_tokens=8192):
 
     x: [M, d_in] CPU tensor (pinned for the copies to overlap; pageable x is pinned first).
     out: optional [M, d_in] pinned CPU tensor of W_dec's dtype to write into.
-    The batch runs in chunks of at most `chunk_tokens` rows on sae's device (halving towards
-    both ends, down to a sixteenth): chunk i+1's host-to-device copy and chunk i-1's device-to-host copy
-    run on their own streams while chunk i is encoded and decoded on the current stream, with
-    two device buffers per direction. One host sync at
-    the end waits for the last copy and reads every chunk's overflow flag; a chunk whose CSR
-    staging overflowed is redone through forward().
+    The batch runs in chunks of at most `chunk_tokens` rows on sae's device: host-to-device
+    copies on one stream, encode and decode on the current stream, device-to-host copies on
+    a third, each chunk starting as soon as its rows have arrived, so only the first chunk's
+    copy in and the last chunk's copy out are not overlapped (the chunk plan keeps those two
+    small). Batches up to WHOLE_BATCH_DEVICE_BYTES get device buffers of their own; larger
+    ones reuse two chunk buffers per direction. One host sync at the end waits for the last
+    copy and reads every chunk's overflow flag; a chunk whose CSR staging overflowed is
+    redone through forward().
     """
     if x.is_cuda:
         raise ValueError("forward_host takes a host tensor; call forward() for a device tensor")
@@ -153,7 +175,7 @@ def forward_host(sae, x, out=None, *, chunk_tokens=8192):
     dev = sae.W_enc.device
     if dev.type != "cuda":
         raise ValueError("the SAE's weights must be on a CUDA device")
-    M, D, dt = x.shape[0], sae.W_dec.shape[1], sae.W_dec.dtype
+    M, K, D, dt = x.shape[0], x.shape[1], sae.W_dec.shape[1], sae.W_dec.dtype
     if out is None:
         out = torch.empty(M, D, dtype=dt, pin_memory=True)
     elif out.is_cuda or tuple(out.shape) != (M, D) or out.dtype != dt:
@@ -164,34 +186,56 @@ def forward_host(sae, x, out=None, *, chunk_tokens=8192):
         x = x.pin_memory()
     compute = torch.cuda.current_stream(dev)
     h2d, d2h = _streams(dev)
-    plan = _chunk_plan(M, chunk_tokens)
-    C = max(plan)
-    xbuf = [torch.empty(C, x.shape[1], dtype=x.dtype, device=dev) for _ in range(2)]
-    obuf = [torch.empty(C, D, dtype=dt, device=dev) for _ in range(2)]
-    ev_in, ev_done, ev_out = [], [], []
-    flags = []
+    whole = M * (K * x.element_size() + D * out.element_size()) <= WHOLE_BATCH_DEVICE_BYTES
+    plan = _chunk_plan(M, chunk_tokens, stream=whole)
+    rows = M if whole else max(plan)
+    nbuf = 1 if whole else 2
+    xbuf = [torch.empty(rows, K, dtype=x.dtype, device=dev) for _ in range(nbuf)]
+    obuf = [torch.empty(rows, D, dtype=dt, device=dev) for _ in range(nbuf)]
+    # the buffers may reuse memory that work queued on the current stream still touches
+    h2d.wait_stream(compute)
+    d2h.wait_stream(compute)
+    bounds = []
     r1 = 0
-    for i, n in enumerate(plan):
-        r0, r1 = r1, r1 + n
-        s = i % 2
-        ev_in.append(torch.cuda.Event())
-        ev_done.append(torch.cuda.Event())
-        ev_out.append(torch.cuda.Event())
+    for n in plan:
+        bounds.append((r1, r1 + n))
+        r1 += n
+
+    def slot(i, r0, r1):  # (x slice, x_hat slice) of chunk i in its device buffer
+        if whole:
+            return xbuf[0][r0:r1], obuf[0][r0:r1]
+        return xbuf[i % 2][:r1 - r0], obuf[i % 2][:r1 - r0]
+
+    ev_in = [torch.cuda.Event() for _ in plan]
+    ev_done = [torch.cuda.Event() for _ in plan]
+    ev_out = [torch.cuda.Event() for _ in plan]
+
+    def copy_in(i):
+        r0, r1 = bounds[i]
         with torch.cuda.stream(h2d):
-            if i >= 2:
-                h2d.wait_event(ev_done[i - 2])  # chunk i-2 has finished reading xbuf[s]
-            xbuf[s][:n].copy_(x[r0:r1], non_blocking=True)
+            if not whole and i >= 2:
+                h2d.wait_event(ev_done[i - 2])  # chunk i-2 has finished reading this buffer
+            slot(i, r0, r1)[0].copy_(x[r0:r1], non_blocking=True)
             ev_in[i].record(h2d)
+
+    if whole:
+        for i in range(len(plan)):  # every copy in is queued at once: the copy engine streams
+            copy_in(i)
+    flags = []
+    for i, (r0, r1) in enumerate(bounds):
+        if not whole:
+            copy_in(i)
+        xs, os_ = slot(i, r0, r1)
         compute.wait_event(ev_in[i])
-        if i >= 2:
-            compute.wait_event(ev_out[i - 2])  # chunk i-2's result has left obuf[s]
-        _, overflow = _forward_async(sae, xbuf[s][:n], obuf[s][:n])
+        if not whole and i >= 2:
+            compute.wait_event(ev_out[i - 2])  # chunk i-2's result has left this buffer
+        _, overflow = _forward_async(sae, xs, os_)
         ev_done[i].record(compute)
         if overflow is not None:
             flags.append((r0, r1, overflow))
         with torch.cuda.stream(d2h):
             d2h.wait_event(ev_done[i])
-            out[r0:r1].copy_(obuf[s][:n], non_blocking=True)
+            out[r0:r1].copy_(os_, non_blocking=True)
             ev_out[i].record(d2h)
     compute.wait_stream(d2h)
     compute.wait_stream(h2d)
