@@ -61,12 +61,6 @@ enum Mode { kDense = 0, kTopk = 1, kCsr = 2 };
 #define SF_RASTER_GROUP_MB 32
 #endif
 constexpr long long kRasterGroupBytes = (long long)SF_RASTER_GROUP_MB << 20;
-// 1: while the CTA pair loads tile t, its TMA warp also prefetches into L2 the W_enc
-// columns of the pair's next tile, one k-block per k-block loaded, so the next tile's
-// first operand loads do not wait on HBM.
-#ifndef SF_PREFETCH_NEXT_W
-#define SF_PREFETCH_NEXT_W 1
-#endif
 
 struct TcParams {
     int M, N, K;
@@ -919,13 +913,6 @@ __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kCon
                 const Unit un = unit_coords(p, u, MODE);
                 for (int nt = 0; ok && nt < un.n_count; ++nt) {
                     const int n_blk = un.n_first + nt;
-                    // this pair's next tile's W_enc columns (-1: none, or the same columns)
-                    int pf_n0 = -1;
-                    if (SF_PREFETCH_NEXT_W) {
-                        const int nxt = nt + 1 < un.n_count ? n_blk + 1
-                                        : (u + npairs < p.num_units ? unit_coords(p, u + npairs, MODE).n_first : -1);
-                        if (nxt >= 0 && nxt != n_blk) pf_n0 = nxt * kBN + (int)rank * HALF_N;
-                    }
                     for (int kb = 0; kb < p.num_kb; ++kb) {
                         if (!wait(&sh->empty[stage], phase ^ 1u)) {
                             ok = false;
@@ -949,14 +936,6 @@ __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kCon
                                                  kb * BK, pol_w);
                         } else {
                             tma_load_2d_pair(b_dst, &tmB, full_leader, kb * BK, n0, pol_w);
-                        }
-                        if (pf_n0 >= 0) {
-                            if (B_MN) {
-#pragma unroll
-                                for (int j = 0; j < HALF_N / MN_BOX; ++j) tma_prefetch_l2_2d(&tmB, pf_n0 + j * MN_BOX, kb * BK);
-                            } else {
-                                tma_prefetch_l2_2d(&tmB, kb * BK, pf_n0);
-                            }
                         }
                         if (++stage == STAGES) {
                             stage = 0;

@@ -183,13 +183,6 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t *bar, uint32_t parity, 
 
 // ---------------------------------------------------------------------------------------
 // TMA (tiled loads into the issuing CTA)
-// Prefetch of a tile of a tensor map into L2 (no shared-memory destination, no barrier).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int32_t c0, int32_t c1) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1)
-                 : "memory");
-}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -223,6 +216,15 @@ __device__ __forceinline__ uint4 ld_nc_v4_hint(const void *ptr, uint64_t policy)
     asm volatile("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(ptr), "l"(policy));
+    return r;
+}
+
+// 16-byte read-only global load that does not allocate in L1 (data used once per SM).
+__device__ __forceinline__ uint4 ld_nc_v4_noalloc(const void *ptr) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ptr));
     return r;
 }
 
