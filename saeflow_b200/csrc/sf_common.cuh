@@ -219,15 +219,6 @@ __device__ __forceinline__ uint4 ld_nc_v4_hint(const void *ptr, uint64_t policy)
     return r;
 }
 
-// 16-byte read-only global load that does not allocate in L1 (data used once per SM).
-__device__ __forceinline__ uint4 ld_nc_v4_noalloc(const void *ptr) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(ptr));
-    return r;
-}
-
 // 16-byte global store with an L2 eviction-priority hint.
 __device__ __forceinline__ void st_global_v4_hint(void *ptr, uint4 v, uint64_t policy) {
     asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "r"(v.x), "r"(v.y),

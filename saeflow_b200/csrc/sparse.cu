@@ -266,15 +266,8 @@ __global__ void compact_kernel(const T *__restrict__ f, int64_t M, int64_t N, in
 #ifndef SF_DECODE_MATH
 #define SF_DECODE_MATH 1  // 0 scalar fmaf per element; 1 packed fp32 FMA per element pair
 #endif
-#ifndef SF_DECODE_ROWS
-#define SF_DECODE_ROWS 2  // gathered W rows in flight per warp step
-#endif
-#ifndef SF_DECODE_L1NA
-#define SF_DECODE_L1NA 0  // 1: W_dec loads skip L1 allocation
-#endif
 __device__ __forceinline__ uint4 ld_w_v4(const void *p, uint64_t pol) {
     if (SF_DECODE_WPOL) return ld_nc_v4_hint(p, pol);
-    if (SF_DECODE_L1NA) return ld_nc_v4_noalloc(p);
     return __ldg(reinterpret_cast<const uint4 *>(p));
 }
 
@@ -359,25 +352,7 @@ __global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restri
         }
         const int n = (end - j0) < 32 ? (int)(end - j0) : 32;
         int t = 0;
-        constexpr int R = SF_DECODE_ROWS;
-        for (; t + R <= n; t += R) {
-            // R rows' loads in flight, then their products in row order (the sum order of
-            // one row at a time)
-            float a[R];
-            uint4 q[R][V];
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int ir = __shfl_sync(0xffffffffu, my_idx, t + r);
-                a[r] = __shfl_sync(0xffffffffu, my_val, t + r);
-                const WT *src = W + (int64_t)ir * ldw + d0 + lane * EPV;
-#pragma unroll
-                for (int v = 0; v < V; ++v)
-                    q[r][v] = active[v] ? ld_w_v4(src + v * 32 * EPV, wpol) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int r = 0; r < R; ++r) fma_vectors<WT, V, NP>(acc, a[r], q[r], active);
-        }
-        for (; t + 1 < n; t += 2) {
+        for (; t + 2 <= n; t += 2) {
             const int i0 = __shfl_sync(0xffffffffu, my_idx, t);
             const int i1 = __shfl_sync(0xffffffffu, my_idx, t + 1);
             const float a0 = __shfl_sync(0xffffffffu, my_val, t);

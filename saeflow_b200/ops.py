@@ -116,34 +116,20 @@ def _even_split(n, cap):
     return [n // k + (1 if i < n % k else 0) for i in range(k)]
 
 
-def _chunk_plan(M, C, stream=True):
-    """Row counts of forward_host's chunks (at most C each).
-
-    Only the first chunk's host-to-device copy and the last chunk's device-to-host copy are
-    exposed; compute per row is ~3x a copy per row (d_in=2304 over PCIe). stream=True (the
-    batch has device buffers of its own, so copies run ahead without waiting for a buffer):
-    C/16 rows at both ends, doubling towards the middle, which is split into equal chunks of
-    at most C and at most 2.5x the ramp's last step (a copy hides as long as each chunk is
-    at most ~2.5x the previous one).
-    stream=False (two device buffers per direction, a chunk's copy waits until the chunk
-    two before it is done): quarter and half chunks at both ends, full chunks between."""
+def _chunk_plan(M, C):
+    """Row counts of forward_host's chunks (at most C each): quarter and half chunks at both
+    ends, full chunks between. Only the first chunk's copy in and the last chunk's copy out
+    are exposed, and every chunk pays a fixed cost (the weights are streamed again, and the
+    scans run again: ~0.1 ms at config 2), so the plan keeps both ends short with few chunks.
+    Measured on B200 at config 2 (16384 rows, C = 8192): 4.66 ms against 3.94 ms with the
+    batch already on the device; plans with more or with smaller end chunks were slower."""
     if M <= C:
         return [M]
-    if not stream:
-        ramp = [max(1, C // 4), max(1, C // 2)]
-        mid = M - 2 * sum(ramp)
-        if mid <= 0:
-            return _even_split(M, C)
-        return ramp + _even_split(mid, C) + ramp[::-1]
-    ramp = [n for n in (C // 16, C // 8, C // 4, C // 2) if n >= 1]
-    while ramp and M - 2 * sum(ramp) <= 0:
-        ramp.pop()
+    ramp = [max(1, C // 4), max(1, C // 2)]
     mid = M - 2 * sum(ramp)
-    if ramp and mid < ramp[-1]:  # fold a short middle into its two neighbours
-        mid += 2 * ramp.pop()
-    if not ramp:
+    if mid <= 0:
         return _even_split(M, C)
-    return ramp + _even_split(mid, min(C, max(1, int(2.5 * ramp[-1])))) + ramp[::-1]
+    return ramp + _even_split(mid, C) + ramp[::-1]
 
 
 # Device bytes (x and x_hat together) up to which forward_host gives the whole batch device
@@ -187,7 +173,7 @@ def forward_host(sae, x, out=None, *, chunk_tokens=8192):
     compute = torch.cuda.current_stream(dev)
     h2d, d2h = _streams(dev)
     whole = M * (K * x.element_size() + D * out.element_size()) <= WHOLE_BATCH_DEVICE_BYTES
-    plan = _chunk_plan(M, chunk_tokens, stream=whole)
+    plan = _chunk_plan(M, chunk_tokens)
     rows = M if whole else max(plan)
     nbuf = 1 if whole else 2
     xbuf = [torch.empty(rows, K, dtype=x.dtype, device=dev) for _ in range(nbuf)]

@@ -403,7 +403,7 @@ def test_forward_host_matches_forward(activation, chunk, whole, monkeypatch):
     from saeflow_b200.ops import _chunk_plan
 
     bounds = [0]
-    for n in _chunk_plan(M, chunk, stream=whole):
+    for n in _chunk_plan(M, chunk):
         bounds.append(bounds[-1] + n)
     want = torch.cat([forward(sae, x[a:b].cuda()).cpu() for a, b in zip(bounds, bounds[1:])])
     whole_out = forward(sae, x.cuda()).cpu()
