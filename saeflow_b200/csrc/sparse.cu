@@ -309,8 +309,11 @@ __device__ __forceinline__ void fma_vectors(float2 (&acc)[V][NP], float a, const
     }
 }
 
+#ifndef SF_DECODE_MIN_BLOCKS
+#define SF_DECODE_MIN_BLOCKS 1  // V <= 2: resident 128-thread blocks per SM the register budget must allow
+#endif
 template <typename WT, typename VT, typename OT, int V>
-__global__ void __launch_bounds__(128) decode_vec_kernel(const int64_t *__restrict__ indptr,
+__global__ void __launch_bounds__(128, V <= 2 ? SF_DECODE_MIN_BLOCKS : 1) decode_vec_kernel(const int64_t *__restrict__ indptr,
                                                          const int32_t *__restrict__ indices,
                                                          const VT *__restrict__ values, const WT *__restrict__ W,
                                                          int64_t ldw, int64_t d_sae, const void *b_dec, int b_dtype,
