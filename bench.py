@@ -366,8 +366,8 @@ def run_ours(args, rank, world, device):
             ev[3].record(stream)
             return out
         launches_per_step = 4  # shift, encode+top-k, merge, decode
-    elif args.route == "dense" or cfg_id == 1:
-        # The reference's route: dense features, then compaction (IEEE fp32 always takes it).
+    elif args.route == "dense":
+        # The reference's route: dense features, then compaction.
         x = make_tokens(cfg_id, rank, device, T)
         row_nnz = torch.zeros(T, dtype=torch.int32, device=device)
 
@@ -552,11 +552,11 @@ def run_ours(args, rank, world, device):
         stages["csr_ms"] = round(mean(csr_ms), 4)
         nnz = step.nnz
         l0 = nnz / T
-        if args.route == "dense" or cfg_id == 1:
+        if args.route == "dense":
             comp_bytes = T * c["d_sae"] * e + nnz * (4 + e) + (T + 1) * 8
             stages["csr_gbps"] = round(comp_bytes / (mean(csr_ms) / 1e3) / 1e9, 1)
         stages["l0"] = round(l0, 2)
-        stages["route"] = "dense+compaction" if (args.route == "dense" or cfg_id == 1) else "encode straight to CSR"
+        stages["route"] = "dense+compaction" if args.route == "dense" else "encode straight to CSR"
     elif cfg_id == 3:
         nnz = csr[1].numel()
         l0 = nnz / T

@@ -128,8 +128,8 @@ SF_API int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_
  * (stage_capacity entries, values in values_dtype) in column order; each row's count is added
  * to row_nnz (caller-zeroed). state[0] (staging cursor) and state[1] (overflow flag) must be
  * zero on entry; state[1] != 0 afterwards means stage_capacity was too small and the staged
- * pairs are incomplete. Workspace: sf_fused_encode_workspace. Tensor-core dtypes only
- * (16-bit W_enc, or fp32 with allow_tf32); IEEE fp32 returns SF_ERR_UNSUPPORTED.
+ * pairs are incomplete. Workspace: sf_fused_encode_workspace. Every dtype: 16-bit W_enc
+ * and fp32 with allow_tf32 on the tensor cores, IEEE fp32 on the CUDA-core encoder.
  * With sf_csr_indptr and sf_csr_place this replaces saeflow/ops.py:36-39 (fused_encode with
  * row_nnz, then dense_to_csr, decode.py:77-94), producing the identical canonical CSR.
  */

@@ -541,8 +541,6 @@ int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vec
     EncodePlan pl;
     st = plan_encode(x, W_enc, allow_tf32, SF_VARIANT_AUTO, &pl);
     if (st) return st;
-    if (!pl.tensor_cores)
-        return set_error(SF_ERR_UNSUPPORTED, "IEEE fp32 encode has no CSR epilogue; use sf_fused_encode");
     const size_t need = plan_workspace(pl);
     if (workspace_bytes < need || (!workspace && need))
         return set_error(SF_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
@@ -554,6 +552,24 @@ int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vec
     if (!pl.fused_x) {
         st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
         if (st) return st;
+    }
+    if (!pl.tensor_cores) {
+        // IEEE fp32: the CUDA-core encoder with the same CSR staging epilogue
+        EpilogueArgs ep{};
+        ep.b_enc = b_enc->data;
+        ep.b_enc_dtype = b_enc->dtype;
+        ep.b_enc_stride = b_enc->stride;
+        if (threshold && threshold->data) {
+            ep.thr = threshold->data;
+            ep.thr_dtype = threshold->dtype;
+            ep.thr_stride = threshold->stride;
+        }
+        ep.activation = activation;
+        ep.out_dtype = values_dtype;
+        ep.row_nnz = row_nnz;
+        CsrArgs csr{tile_counts, tile_offsets, stage_indices, stage_values, state, (unsigned)stage_capacity};
+        return encode_simt_f32(static_cast<const float *>(xs), pl.a_pitch, static_cast<const float *>(W_enc->data),
+                               W_enc->stride_row, W_enc->stride_col, M, N, K, ep, s, &csr);
     }
     GemmOperands g{};
     set_a_operand(g, pl, x, b_dec, xs);

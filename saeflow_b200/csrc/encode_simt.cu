@@ -2,7 +2,8 @@
 //
 // The reference computes fp32 inputs with `input_precision="ieee"` unless TF32 is
 // allowed (saeflow/kernels/encode.py:118-120); this kernel is that path. Epilogue
-// semantics are identical to the tensor-core kernel (encode.py:195-208).
+// semantics are identical to the tensor-core kernel (encode.py:77-91), including the
+// encode-straight-to-CSR staging epilogue (CSR = true).
 //
 // 128 x (64*NF) output tile per CTA, K in steps of 8 through double-buffered shared memory,
 // 256 threads each owning an 8 x (4*NF) register block (rows {4ty..4ty+3, 64+4ty..}, columns
@@ -40,10 +41,97 @@ __device__ __forceinline__ void simt_store4(void *out, int64_t sm, int64_t sn, i
         if (col + j < N) base[(int64_t)(col + j) * sn] = from_f32<OT>(v[j]);
 }
 
-template <int NF>
-__global__ void __launch_bounds__(SB_T, NF == 2 ? 2 : 1)
+// Inclusive sum over the 16 lanes of this half-warp (lanes 0-15 or 16-31).
+__device__ __forceinline__ int half_warp_inclusive_scan(int v, int tx) {
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, off, 16);
+        if (tx >= off) v += t;
+    }
+    return v;
+}
+
+// Encode straight to CSR (256-column tiles): for each of its 8 rows a thread holds 16
+// stored values (columns 64h + 4tx + j); the 16 threads of a row are one half-warp. Nonzero
+// masks are taken on the stored value, as the dense route counts them. Within a row, offsets
+// follow column order (h, then tx, then j) by four half-warp scans; one atomicAdd per warp
+// reserves staging space for its 16 rows (ordered i, half), and each (row, tile) cell gets its
+// count and, when nonzero, its staging offset: the staging contract of the tensor-core
+// kernel's CSR epilogue, consumed by the same placement kernel.
+template <typename VT>
+__device__ __forceinline__ void simt_csr_epilogue(const float (&o)[8][16], int m0, int n0, int M, int N, int tx,
+                                                  int ty, const EpilogueArgs &ep, const CsrArgs &csr,
+                                                  int n_tiles) {
+    const int lane = threadIdx.x & 31;
+    const int tile = n0 / kCsrTile;
+    int tot[8], pre[8][4];
+    uint32_t mask[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + ((i < 4) ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        uint32_t m = 0;
+#pragma unroll
+        for (int h = 0; h < 4; ++h)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                m |= ((o[i][h * 4 + j] != 0.f && n0 + h * 64 + tx * 4 + j < N && row < M) ? 1u : 0u)
+                     << (h * 4 + j);
+        mask[i] = m;
+        int run = 0;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const int c = __popc((m >> (h * 4)) & 0xFu);
+            const int incl = half_warp_inclusive_scan(c, tx);
+            pre[i][h] = run + incl - c;
+            run += __shfl_sync(0xffffffffu, incl, 15, 16);
+        }
+        tot[i] = run;
+    }
+    // One reservation per warp: its rows ordered (i, half), half = lane / 16.
+    const int half = lane >> 4;
+    int warp_total = 0, my_off[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int t0 = __shfl_sync(0xffffffffu, tot[i], 0);
+        const int t1 = __shfl_sync(0xffffffffu, tot[i], 16);
+        my_off[i] = warp_total + (half ? t0 : 0);
+        warp_total += t0 + t1;
+    }
+    unsigned base = 0;
+    if (lane == 0 && warp_total > 0) base = atomicAdd(&csr.state[0], (unsigned)warp_total);
+    base = __shfl_sync(0xffffffffu, base, 0);
+    const bool fits = (unsigned long long)base + (unsigned long long)warp_total <= (unsigned long long)csr.cap;
+    if (lane == 0 && warp_total > 0 && !fits) atomicOr(&csr.state[1], 1u);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int row = m0 + ((i < 4) ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        const unsigned row_off = base + (unsigned)my_off[i];
+        if (tx == 0 && row < M) {
+            const int64_t cell = (int64_t)row * n_tiles + tile;
+            csr.tile_cnt[cell] = tot[i];
+            if (tot[i]) csr.tile_off[cell] = (int)row_off;
+            if (ep.row_nnz != nullptr && tot[i]) atomicAdd(ep.row_nnz + row, tot[i]);
+        }
+        if (!fits || mask[i] == 0) continue;
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            unsigned at = row_off + (unsigned)pre[i][h];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (mask[i] & (1u << (h * 4 + j))) {
+                    csr.stage_idx[at] = n0 + h * 64 + tx * 4 + j;
+                    reinterpret_cast<VT *>(csr.stage_val)[at] = from_f32<VT>(o[i][h * 4 + j]);
+                    ++at;
+                }
+            }
+        }
+    }
+}
+
+template <int NF, bool CSR>
+__global__ void __launch_bounds__(SB_T, 1)
     encode_simt_kernel(const float *__restrict__ xs, int64_t ldx, const float *__restrict__ W, int64_t swk,
-                       int64_t swn, int M, int N, int K, EpilogueArgs ep, int w_vec) {
+                       int64_t swn, int M, int N, int K, EpilogueArgs ep, int w_vec, CsrArgs csr, int n_tiles) {
     constexpr int SB_N = 64 * NF;
     constexpr int BQ = NF / 2;  // float4 loads of the B tile per thread per K step
     __shared__ __align__(16) float As[2][SB_K][SB_M + 4];
@@ -132,6 +220,30 @@ __global__ void __launch_bounds__(SB_T, NF == 2 ? 2 : 1)
         __syncthreads();
     }
 
+    if constexpr (CSR) {
+        static_assert(NF == 4, "CSR staging needs 256-column tiles");
+        // bias, activation and rounding in place, then the staging epilogue
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int h = 0; h < NF; ++h)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int c = h * 64 + tx * 4 + j;
+                    const float pre = acc[i][h * 4 + j] + s_bias[c];
+                    float o = fmaxf(pre, 0.f);
+                    if (ep.activation == SF_ACT_JUMPRELU) o = (pre > s_thr[c]) ? o : 0.f;
+                    acc[i][h * 4 + j] = round_to(o, ep.out_dtype);
+                }
+        if (ep.out_dtype == SF_F32)
+            simt_csr_epilogue<float>(acc, m0, n0, M, N, tx, ty, ep, csr, n_tiles);
+        else if (ep.out_dtype == SF_BF16)
+            simt_csr_epilogue<__nv_bfloat16>(acc, m0, n0, M, N, tx, ty, ep, csr, n_tiles);
+        else
+            simt_csr_epilogue<__half>(acc, m0, n0, M, N, tx, ty, ep, csr, n_tiles);
+        return;
+    } else {
+
     // Epilogue: bias, activation, rounding to the output dtype, count, store.
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -165,22 +277,29 @@ __global__ void __launch_bounds__(SB_T, NF == 2 ? 2 : 1)
         for (int off = 8; off > 0; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
         if (tx == 0 && ep.row_nnz != nullptr && row < M && cnt != 0) atomicAdd(ep.row_nnz + row, cnt);
     }
+    }  // dense epilogue
 }
 
 }  // namespace
 
 int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
-                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream) {
-    const bool wide = N >= 256;
+                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream, const CsrArgs *csr) {
+    const bool wide = N >= 256 || csr != nullptr;  // CSR staging needs whole 256-column tiles
     const int64_t sb_n = wide ? 256 : 128;
     if ((N + sb_n - 1) / sb_n > 2147483647ll || (M + SB_M - 1) / SB_M > 65535)
         return set_error(SF_ERR_UNSUPPORTED, "SIMT encode grid too large (M=%lld N=%lld)", (long long)M, (long long)N);
     const int w_vec = (swn == 1 && (swk % 4) == 0 && (reinterpret_cast<uintptr_t>(W) & 15u) == 0) ? 1 : 0;
     dim3 grid((unsigned)((N + sb_n - 1) / sb_n), (unsigned)((M + SB_M - 1) / SB_M));
-    if (wide)
-        encode_simt_kernel<4><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec);
+    const int n_tiles = (int)((N + kCsrTile - 1) / kCsrTile);
+    if (csr)
+        encode_simt_kernel<4, true><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep,
+                                                               w_vec, *csr, n_tiles);
+    else if (wide)
+        encode_simt_kernel<4, false><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K,
+                                                                ep, w_vec, CsrArgs{}, n_tiles);
     else
-        encode_simt_kernel<2><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec);
+        encode_simt_kernel<2, false><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K,
+                                                                ep, w_vec, CsrArgs{}, n_tiles);
     return check_cuda(cudaGetLastError(), "encode_simt launch");
 }
 

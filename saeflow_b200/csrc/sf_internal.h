@@ -85,7 +85,9 @@ int encode_tc_topk(const GemmOperands &g, const TopkArgs &tk, cudaStream_t strea
 int topk_chunks(int64_t M, int64_t N);
 constexpr int kTopkMaxK = 112;  // shared-memory bound of the fused top-k lists and candidate buffers
 
+// IEEE fp32 encoder on the CUDA cores: dense output (csr == nullptr) or the CSR staging of
+// encode_tc_csr (same tile counts, offsets and column-ordered runs).
 int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
-                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream);
+                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream, const CsrArgs *csr = nullptr);
 
 }  // namespace sf

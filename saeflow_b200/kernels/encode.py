@@ -123,9 +123,10 @@ def encode_csr(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *, all
 
     Returns exactly `dense_to_csr(fused_encode(..., row_nnz=r), r)` (the reference's
     encode_sparse, saeflow/ops.py:36-39): the GEMM epilogue stages each row's nonzeros per
-    256-column tile and a placement kernel writes the canonical CSR after the one host sync
-    that sizes it. IEEE fp32 (no tensor cores) and a staging overflow (more nonzeros than
-    `stage_capacity`, default min(d_sae, 512) per row) take the dense route instead.
+    256-column tile (the tensor-core encoder, or the CUDA-core one for IEEE fp32) and a
+    placement kernel writes the canonical CSR after the one host sync that sizes it. A
+    staging overflow (more nonzeros than `stage_capacity`, default min(d_sae, 512) per row)
+    takes the dense route instead.
     """
     staged = encode_csr_stage(x, W_enc, b_enc, b_dec, threshold, activation, allow_tf32=allow_tf32,
                               stage_capacity=stage_capacity)
@@ -160,7 +161,7 @@ def encode_csr_stage(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", 
     h = _Staged()
     h.args = (x, W_enc, b_enc, b_dec, threshold, activation, allow_tf32)
     h.dev, h.M, h.N, h.dtype, h.csr = dev, M, N, x.dtype, None
-    if M == 0 or not _uses_tensor_cores(x, W_enc, allow_tf32, _abi.SF_VARIANT_AUTO):
+    if M == 0:
         h.csr = _dense_route(h)
         return h
     n_tiles = (N + _abi.CSR_TILE - 1) // _abi.CSR_TILE

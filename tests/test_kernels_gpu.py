@@ -265,11 +265,12 @@ def _assert_same_csr(a, b):
         assert torch.equal(bits(u), bits(v))
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("activation", ["relu", "jumprelu"])
 @pytest.mark.parametrize("shape", [(1, 16, 32), (37, 50, 129), (300, 128, 1000), (700, 256, 4099), (2000, 512, 8192)])
 def test_encode_csr_identical_to_dense_route(dtype, activation, shape):
-    """Encode straight to CSR gives bit-for-bit the CSR of fused_encode + dense_to_csr."""
+    """Encode straight to CSR gives bit-for-bit the CSR of fused_encode + dense_to_csr
+    (fp32: the CUDA-core encoder's staging epilogue, IEEE products)."""
     M, d_in, d_sae = shape
     sae = make_sae(d_in, d_sae, activation, dtype).to("cuda")
     if activation == "relu":
@@ -319,6 +320,20 @@ def test_encode_csr_values_that_round_to_zero(dtype):
         got = encode_csr(x, W, b_enc, b_dec, thr, act)
         _assert_same_csr(got, want)
     assert int(want[1].numel()) > 0
+
+
+def test_encode_csr_fp32_overflow_and_strided_weights():
+    """IEEE fp32 staging: a capacity too small is detected and redone densely, and a
+    column-major W_enc gives the same CSR as the dense route."""
+    sae = make_sae(96, 700, "relu", torch.float32).to("cuda")
+    sae.b_enc[:] = -5.0
+    sae.b_enc[:300] = 5.0
+    x = torch.randn(300, 96, device="cuda")
+    W = sae.W_enc.T.contiguous().T
+    rn = torch.zeros(300, device="cuda", dtype=torch.int32)
+    want = dense_to_csr(fused_encode(x, W, sae.b_enc, sae.b_dec, row_nnz=rn), rn)
+    _assert_same_csr(encode_csr(x, W, sae.b_enc, sae.b_dec), want)
+    _assert_same_csr(encode_csr(x, W, sae.b_enc, sae.b_dec, stage_capacity=1000), want)
 
 
 def test_encode_csr_strided_inputs_and_empty():
