@@ -183,6 +183,8 @@ __device__ __forceinline__ void stage_bias(const TcParams &p, TcShared *sh, int 
             if (mode == kCsr) t = p.activation == SF_ACT_JUMPRELU ? (t != t ? __int_as_float(0x7f800000) : fmaxf(t, zc)) : zc;
         } else if (mode == kCsr) {
             t = __int_as_float(0x7f800000);  // +inf: columns past d_sae never fire
+        } else if (mode == kTopk) {
+            b = __int_as_float(0xff800000);  // -inf: columns past d_sae never enter a top-k list
         }
         sh->bias[buf][j] = b;
         sh->thr[buf][j] = t;
@@ -361,6 +363,24 @@ __device__ __noinline__ TopkState topk_merge_buffer(unsigned long long *lists, c
 constexpr int kTopkGroup = 8;
 __device__ __forceinline__ void topk_chunk(const TcParams &p, const float *bias, const uint32_t (&r)[32], int col0,
                                            unsigned long long *topk_lists, int et, TopkState &ts) {
+    // pre-activations of the chunk (bias read as float4; -inf past d_sae) and their maximum:
+    // once the lists are full, most chunks hold no column above any of the warp's 32 running
+    // k-th values, and the whole chunk is skipped on that one test.
+    float pre[32];
+    float mx = __int_as_float(0xff800000);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 b4 = *reinterpret_cast<const float4 *>(bias + j);
+        pre[j + 0] = __uint_as_float(r[j + 0]) + b4.x;
+        pre[j + 1] = __uint_as_float(r[j + 1]) + b4.y;
+        pre[j + 2] = __uint_as_float(r[j + 2]) + b4.z;
+        pre[j + 3] = __uint_as_float(r[j + 3]) + b4.w;
+        mx = fmaxf(mx, fmaxf(fmaxf(pre[j], pre[j + 1]), fmaxf(pre[j + 2], pre[j + 3])));
+    }
+    // relu(pre) > min_val needs pre > min_val when min_val >= 0 (NaN pre stores 0 and never
+    // enters then); while a list is filling (min_val = -1) every column below d_sae enters
+    const bool need = col0 < p.N && (ts.min_val < 0.f || mx > ts.min_val);
+    if (!__any_sync(0xffffffffu, need)) return;
     unsigned long long *buf = topk_lists + p.k * 128;
 #pragma unroll
     for (int g = 0; g < 32; g += kTopkGroup) {
@@ -368,7 +388,7 @@ __device__ __forceinline__ void topk_chunk(const TcParams &p, const float *bias,
 #pragma unroll
         for (int j = g; j < g + kTopkGroup; ++j) {
             const int col = col0 + j;
-            const float o = fmaxf(__uint_as_float(r[j]) + bias[j], 0.f);
+            const float o = fmaxf(pre[j], 0.f);
             if (o > min_val && col < p.N) {
                 const float v = round_to(o, p.values_dtype);
                 buf[ts.cnt * 128 + et] =
