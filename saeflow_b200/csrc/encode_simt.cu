@@ -19,6 +19,12 @@ namespace sf {
 namespace {
 
 constexpr int SB_M = 128, SB_K = 8, SB_T = 256;
+// K steps of one shared-memory tile unrolled at once: each is 8 x 4NF FMAs, and the fully
+// unrolled tile body (8 steps, ~1000 FMAs) overflows the instruction cache.
+#ifndef SF_SIMT_KK_UNROLL
+#define SF_SIMT_KK_UNROLL 8
+#endif
+constexpr int kKkUnroll = SF_SIMT_KK_UNROLL;
 
 template <typename OT>
 __device__ __forceinline__ void simt_store4(void *out, int64_t sm, int64_t sn, int vec, int64_t N, int row, int col,
@@ -200,7 +206,7 @@ __global__ void __launch_bounds__(SB_T, 1)
     for (int kt = 0; kt < nk; ++kt) {
         const int buf = kt & 1;
         if (kt + 1 < nk) load_tile((kt + 1) * SB_K);
-#pragma unroll
+#pragma unroll kKkUnroll
         for (int kk = 0; kk < SB_K; ++kk) {
             const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][kk][ty * 4]);
             const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][kk][64 + ty * 4]);

@@ -11,7 +11,9 @@ properties are checked on every row at full size:
   forward == decode(encode_sparse);
 * config 3 (decode only): every row against the oracle;
 * config 4 (TopK k=32): the selected values are the dense ReLU encoder's values at the
-  selected ids, and no other feature of the row ranks above the k-th (value, then lower id).
+  selected ids, and no other feature of the row ranks above the k-th (value, then lower id);
+* config 5's feature dimension (d_sae = 2^20) on a 4096-token slice of its batch: encode
+  straight to CSR equals the dense route bit for bit, forward == decode(encode_sparse).
 
 The tolerances are oracle/contract.py's: rtol 1e-2 (bf16) / 1e-5 (fp32) with small
 absolute floors, features within 1e-3 of their cut excluded, CSR structure bit-exact.
@@ -189,3 +191,23 @@ def test_cfg4_topk_bf16_full_size():
     out = saeflow_b200.forward(sae, x)
     ip = torch.arange(0, rows.numel() * k + 1, k, dtype=torch.int64)
     check_decoded_rows(sae, out, (ip, idx[rows].cpu().flatten(), vals[rows].cpu().flatten()), rows)
+
+
+def test_cfg5_jumprelu_2pow20_features_token_slice():
+    dev = torch.device("cuda")
+    sae = bench.make_sae_cfg5(dev, 0, 1 << 20)
+    x = bench.make_token_range(5, 0, 4096, dev)
+    T = x.shape[0]
+    csr = saeflow_b200.encode_sparse(sae, x)
+    rn = torch.zeros(T, dtype=torch.int32, device=dev)
+    f = fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, "jumprelu", row_nnz=rn)
+    assert_same_csr(csr, dense_to_csr(f, rn))
+    l0 = csr[1].numel() / T
+    assert 85 < l0 < 115, f"L0 {l0}"  # the config's thresholds give L0 ~ 96
+    out = saeflow_b200.forward(sae, x)
+    assert torch.equal(bits(out), bits(sparse_decode(*csr, sae.W_dec, sae.b_dec)))
+
+    rows = sample_rows(T, 64)
+    check_encoded_rows(sae, x, f[rows], csr, rows)
+    del f
+    check_decoded_rows(sae, out, sub_csr(csr, rows), rows)
