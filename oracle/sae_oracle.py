@@ -134,8 +134,10 @@ def dense_to_csr(f, row_nnz=None):
 def sparse_decode(indptr, indices, values, W_dec, b_dec=None, out_dtype=None):
     """b_dec + sum_j values[j] * W_dec[indices[j]] per row (decode.py:28-55), float64 sums.
 
-    The row sums are one float64 CSR x dense product (the sum order does not matter at
-    float64 precision for these checks); only indptr's ranges of indices / values are read."""
+    The row sums are one float64 CSR x dense product over the W_dec rows the CSR references
+    (gathered and renumbered first, so a 2^20-row W_dec is never widened whole); the sum
+    order does not matter at float64 precision for these checks. Only indptr's ranges of
+    indices / values are read."""
     M = indptr.numel() - 1
     D, N = W_dec.shape[1], W_dec.shape[0]
     ip = indptr.long()
@@ -145,9 +147,10 @@ def sparse_decode(indptr, indices, values, W_dec, b_dec=None, out_dtype=None):
         idx = indices[:nnz].long()
         if int(idx.min()) < 0 or int(idx.max()) >= N:
             raise ValueError("sparse_decode: an index is outside W_dec's rows")
+        used, local = torch.unique(idx, return_inverse=True)
         with torch.sparse.check_sparse_tensor_invariants(False):
-            csr = torch.sparse_csr_tensor(ip, idx, values[:nnz].double(), (M, N))
-            acc += torch.sparse.mm(csr, W_dec.double())
+            csr = torch.sparse_csr_tensor(ip, local, values[:nnz].double(), (M, used.numel()))
+            acc += torch.sparse.mm(csr, W_dec[used].double())
     if b_dec is not None:
         acc += b_dec.double()
     return acc.to(out_dtype or W_dec.dtype)
