@@ -55,9 +55,9 @@ enum sf_status {
 
 /* Encode variant selector (the `config=` kwarg of fused_encode).                  */
 enum sf_encode_variant {
-    SF_VARIANT_AUTO = 0,     /* tensor cores for 16-bit / TF32, CUDA cores for IEEE fp32 */
+    SF_VARIANT_AUTO = 0,     /* tcgen05/TMEM kernel (IEEE fp32: split operands up to d_in 1024, CUDA cores above) */
     SF_VARIANT_TCGEN05 = 1,  /* force the tcgen05/TMEM kernel (CTA pairs when M > 128) */
-    SF_VARIANT_SIMT = 2,     /* force the CUDA-core kernel                           */
+    SF_VARIANT_SIMT = 2,     /* force the CUDA-core kernel (fp32 W_enc only)          */
     SF_VARIANT_TCGEN05_SINGLE = 3  /* tcgen05 kernel on single CTAs (128 x 256 tiles)  */
 };
 
@@ -96,7 +96,10 @@ SF_API int sf_device_error(uint32_t *code);
 /*
  * Workspace bytes sf_fused_encode needs for these operands (the b_dec-shifted,
  * dtype-converted copy of x, plus a repacked W_enc when its layout cannot be read by
- * TMA). Replaces the allocation-free Triton launch of saeflow/kernels/encode.py:115-139.
+ * TMA; for IEEE fp32 on the tensor cores the three-part bf16 splits of the shifted x and of
+ * W_enc, 6 d_in' bytes per row and 6 d_in' bytes per feature with d_in' = d_in rounded up
+ * to 64, plus 4 d_in bytes per row for the non-finite fallback). Replaces the
+ * allocation-free Triton launch of saeflow/kernels/encode.py:115-139.
  */
 SF_API int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int allow_tf32,
                               int variant, size_t *bytes);
@@ -110,7 +113,15 @@ SF_API int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc,
  *   out    [M, d_sae] in out->dtype, any strides (data is written through)
  *   row_nnz: NULL or int32 [M]; each row's count of stored nonzeros is ADDED
  *            (encode.py:89-91; the buffer is caller-zeroed)
- *   allow_tf32: fp32 W_enc only; 0 = IEEE fp32 products (encode.py:118-120)
+ *   allow_tf32: fp32 W_enc only; 0 = IEEE fp32 products (encode.py:118-120). With fp32 x
+ *            too these run on the bf16 tensor cores by default: both operands split into
+ *            three bf16 parts (Henry, Tang & Heinecke, ARITH 2019), the six partial products
+ *            above 2^-23 summed smallest first in the fp32 accumulator. The tensor cores
+ *            round that sum toward zero once per 16 products, an error growing with d_in:
+ *            at d_in 768 it matches fp32 FMA chains, so SF_VARIANT_AUTO takes this route up
+ *            to d_in 1024 and the CUDA-core IEEE kernel beyond (SF_VARIANT_TCGEN05 forces the
+ *            split route, SF_VARIANT_SIMT the CUDA-core kernel). An inf or NaN operand makes
+ *            the call run on the CUDA-core kernel instead (decided on the device, no sync).
  */
 SF_API int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
                     const sf_vector *b_dec, const sf_vector *threshold, int activation,
@@ -128,8 +139,8 @@ SF_API int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_
  * (stage_capacity entries, values in values_dtype) in column order; each row's count is added
  * to row_nnz (caller-zeroed). state[0] (staging cursor) and state[1] (overflow flag) must be
  * zero on entry; state[1] != 0 afterwards means stage_capacity was too small and the staged
- * pairs are incomplete. Workspace: sf_fused_encode_workspace. Every dtype: 16-bit W_enc
- * and fp32 with allow_tf32 on the tensor cores, IEEE fp32 on the CUDA-core encoder.
+ * pairs are incomplete. Workspace: sf_fused_encode_workspace. Every dtype on the tensor
+ * cores (IEEE fp32 from split operands, with the CUDA-core fallback for non-finite ones).
  * With sf_csr_indptr and sf_csr_place this replaces saeflow/ops.py:36-39 (fused_encode with
  * row_nnz, then dense_to_csr, decode.py:77-94), producing the identical canonical CSR.
  */
@@ -208,9 +219,11 @@ SF_API int sf_sparse_decode(const int64_t *indptr, int64_t M, const int32_t *ind
  * whose sf_fused_encode_workspace exceeds 16 MiB are rejected with SF_ERR_WORKSPACE
  * (e.g. bf16 x with d_in=2304: at most 3640 rows per call). W_enc must be readable in
  * place: a 16-bit W_enc contiguous along one dimension with a 16-byte-aligned base and
- * row pitch, or on the TF32 path an fp32 W_enc in column-major layout (or the IEEE fp32
- * path, which never copies W_enc); other layouts need a repacked copy of W_enc that the
- * scratch cannot hold, and are rejected with their own message. The first call on a
+ * row pitch, or on the TF32 path an fp32 W_enc in column-major layout; other layouts need a
+ * repacked copy of W_enc that the scratch cannot hold, and are rejected with their own
+ * message. IEEE fp32 (fp32 x and W_enc, allow_tf32 0) with SF_VARIANT_AUTO runs on the
+ * CUDA-core kernel here, which reads W_enc in place: the tensor-core route's split copy of
+ * W_enc does not fit the scratch. The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress) and should come
  * before any stream capture; the address is kept for the process's life, so calls after
  * a cudaDeviceReset of that device are unsupported. Every call on a device shares the one

@@ -1,6 +1,7 @@
 // extern "C" entry points of libsaeflow_b200.so: argument validation, workspace layout,
 // kernel selection. The entry points mirror the host wrappers of saeflow/kernels
 // (encode.py:97-139, decode.py:77-126) one level down: the caller owns every buffer.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -91,7 +92,8 @@ namespace {
 template <typename XT, typename MT>
 __global__ void shift_convert_kernel(const XT *__restrict__ x, int64_t M, int64_t K, int64_t sxm, int64_t sxk,
                                      const void *b_dec, int b_dtype, int64_t b_stride, MT *__restrict__ xs,
-                                     int64_t pitch) {
+                                     int64_t pitch, const unsigned *gate) {
+    if (gate != nullptr && *reinterpret_cast<const volatile unsigned *>(gate) == 0u) return;
     constexpr int EPV = 16 / sizeof(MT);
     const int64_t vec_per_row = pitch / EPV;
     const int64_t total = M * vec_per_row;
@@ -119,7 +121,8 @@ __global__ void shift_convert_kernel(const XT *__restrict__ x, int64_t M, int64_
 template <typename XT, typename MT>
 __global__ void shift_convert_vec_kernel(const XT *__restrict__ x, int64_t M, int64_t K, int64_t sxm,
                                          const void *b_dec, int b_dtype, int64_t b_stride, MT *__restrict__ xs,
-                                         int64_t pitch) {
+                                         int64_t pitch, const unsigned *gate) {
+    if (gate != nullptr && *reinterpret_cast<const volatile unsigned *>(gate) == 0u) return;
     constexpr int EPV = 8;  // elements per work item (16 B of 16-bit, 32 B of fp32)
     const int64_t items_per_row = pitch / EPV;
     const int64_t total = M * items_per_row;
@@ -253,6 +256,12 @@ struct EncodePlan {
     int64_t w_pitch; // pitch of W_enc as TMA sees it (elements)
     size_t xs_bytes, wp_bytes;
     bool fused_x;    // the CTA-pair kernel's converter warps read x itself and shift it (no copy)
+    // IEEE fp32 on the bf16 tensor cores (emulate.cu). Workspace: the split x [M, 3 kp] bf16,
+    // then (at xs32_off) the fp32 shifted x of the non-finite fallback, then the fallback
+    // flag (at flag_off), then the split W_enc [3 kp, w_pitch] bf16.
+    bool emulate;
+    int64_t kp, xs32_pitch;
+    size_t xs32_off, flag_off;
 };
 
 int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int variant, EncodePlan *pl) {
@@ -261,11 +270,15 @@ int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int vari
     if (variant < SF_VARIANT_AUTO || variant > SF_VARIANT_TCGEN05_SINGLE)
         return set_error(SF_ERR_INVALID, "unknown encode variant %d", variant);
     bool tc;
+    pl->emulate = false;
     if (wdt == SF_F32) {
-        const bool tf32 = allow_tf32 || x->dtype != SF_F32;
-        tc = tf32;
-        if (variant == SF_VARIANT_TCGEN05 || variant == SF_VARIANT_TCGEN05_SINGLE) tc = true;
-        if (variant == SF_VARIANT_SIMT) tc = false;
+        // IEEE products (fp32 x, TF32 not allowed) run split-precision on the bf16 tensor
+        // cores when asked for (a tcgen05 variant) or, under AUTO, up to kEmuMaxAutoK;
+        // otherwise on the CUDA-core kernel. TF32 products on the tensor cores.
+        const bool ieee = !allow_tf32 && x->dtype == SF_F32;
+        tc = variant != SF_VARIANT_SIMT;
+        if (ieee && variant == SF_VARIANT_AUTO && K > kEmuMaxAutoK) tc = false;
+        pl->emulate = ieee && tc;
     } else {
         tc = true;
         if (variant == SF_VARIANT_SIMT)
@@ -290,6 +303,21 @@ int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int vari
     pl->w_direct = true;
     pl->b_mn = true;
     pl->w_pitch = 0;
+    if (pl->emulate) {
+        pl->ab_fmt = 1;
+        pl->mma_dtype = SF_BF16;
+        pl->kp = round_up(K > 0 ? K : 1, kEmuKBlock);
+        pl->a_pitch = 3 * pl->kp;
+        pl->xs32_pitch = round_up(K > 0 ? K : 1, 8);
+        pl->xs32_off = (size_t)round_up(M * pl->a_pitch * 2, 256);
+        pl->flag_off = pl->xs32_off + (size_t)round_up(M * pl->xs32_pitch * 4, 256);
+        pl->xs_bytes = pl->flag_off + 256;
+        pl->w_direct = false;
+        pl->b_mn = true;
+        pl->w_pitch = round_up(N > 0 ? N : 1, 8);
+        pl->wp_bytes = (size_t)(3 * pl->kp * pl->w_pitch * 2);
+        return SF_OK;
+    }
     if (tc && wdt == SF_F32) {
         // 32-bit operands: feed W_enc K-major (in place when it is column-major).
         pl->b_mn = false;
@@ -341,7 +369,9 @@ void set_a_operand(GemmOperands &g, const EncodePlan &pl, const sf_matrix *x, co
     }
 }
 
-int run_shift_convert(const sf_matrix *x, const sf_vector *b_dec, int mdt, void *xs, int64_t pitch, cudaStream_t s) {
+// gate: non-null makes the pass a no-op unless *gate is nonzero at run time.
+int run_shift_convert(const sf_matrix *x, const sf_vector *b_dec, int mdt, void *xs, int64_t pitch, cudaStream_t s,
+                      const unsigned *gate = nullptr) {
     const int64_t M = x->rows, K = x->cols;
     if (M == 0) return SF_OK;
     const void *bp = (b_dec && b_dec->data) ? b_dec->data : nullptr;
@@ -354,16 +384,18 @@ int run_shift_convert(const sf_matrix *x, const sf_vector *b_dec, int mdt, void 
             const int64_t xe = sizeof(XT);
             const bool vec = x->stride_col == 1 && (x->stride_row * xe) % 16 == 0 && aligned16(x->data) &&
                              (K % (16 / xe)) == 0;
+            // A gated pass (a no-op unless a flag is set) runs on one CTA per SM, grid-stride.
+            auto grid = [&](int64_t items) { return gate ? std::min<unsigned>(grid_for(items), num_sms()) : grid_for(items); };
             if (vec) {
                 const int64_t items = M * (pitch / 8);
-                shift_convert_vec_kernel<XT, MT><<<grid_for(items), 256, 0, s>>>(
+                shift_convert_vec_kernel<XT, MT><<<grid(items), 256, 0, s>>>(
                     reinterpret_cast<const XT *>(x->data), M, K, x->stride_row, bp, bdt, bs,
-                    reinterpret_cast<MT *>(xs), pitch);
+                    reinterpret_cast<MT *>(xs), pitch, gate);
             } else {
                 const int64_t items = M * (pitch / (16 / (int64_t)sizeof(MT)));
-                shift_convert_kernel<XT, MT><<<grid_for(items), 256, 0, s>>>(
+                shift_convert_kernel<XT, MT><<<grid(items), 256, 0, s>>>(
                     reinterpret_cast<const XT *>(x->data), M, K, x->stride_row, x->stride_col, bp, bdt, bs,
-                    reinterpret_cast<MT *>(xs), pitch);
+                    reinterpret_cast<MT *>(xs), pitch, gate);
             }
             return check_cuda(cudaGetLastError(), "shift_convert launch");
         });
@@ -386,6 +418,84 @@ int run_repack(const sf_matrix *W, void *wp, int64_t pitch, bool mn_major, cudaS
                                                              pitch);
         return check_cuda(cudaGetLastError(), "repack launch");
     });
+}
+
+// Pre-passes of a tensor-core plan and the GEMM operands they leave in the workspace: the
+// operand split (split-precision fp32), or the shifted copy of x and, when TMA cannot read
+// W_enc in place, its repacked copy.
+int prepare_tc(const EncodePlan &pl, const sf_matrix *x, const sf_matrix *W, const sf_vector *b_dec, uint8_t *ws,
+               cudaStream_t s, GemmOperands &g) {
+    g = GemmOperands{};
+    g.M = x->rows;
+    g.N = W->cols;
+    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
+    if (pl.emulate) {
+        EmuOperands e{};
+        e.x = static_cast<const float *>(x->data);
+        e.M = x->rows;
+        e.K = x->cols;
+        e.sxm = x->stride_row;
+        e.sxk = x->stride_col;
+        if (b_dec && b_dec->data) {
+            e.b_dec = b_dec->data;
+            e.b_dtype = b_dec->dtype;
+            e.b_stride = b_dec->stride;
+        }
+        e.W = static_cast<const float *>(W->data);
+        e.N = W->cols;
+        e.swk = W->stride_row;
+        e.swn = W->stride_col;
+        e.a = reinterpret_cast<__nv_bfloat16 *>(ws);
+        e.b = static_cast<__nv_bfloat16 *>(wp);
+        e.kp = pl.kp;
+        e.b_pitch = pl.w_pitch;
+        e.flag = reinterpret_cast<unsigned *>(ws + pl.flag_off);
+        const int st = emu_split_operands(e, s);
+        if (st) return st;
+        g.a = ws;
+        g.a_pitch = pl.a_pitch;
+        g.b = wp;
+        g.b_pitch = pl.w_pitch;
+        g.b_mn_major = true;
+        g.ab_fmt = 1;
+        g.K = 3 * pl.kp;
+        g.seg_kb = (int)(pl.kp / kEmuKBlock);
+        g.seg_a = kEmuSegA;
+        g.seg_b = kEmuSegB;
+        g.skip = e.flag;
+        return SF_OK;
+    }
+    if (!pl.fused_x) {
+        const int st = run_shift_convert(x, b_dec, pl.mma_dtype, ws, pl.a_pitch, s);
+        if (st) return st;
+    }
+    set_a_operand(g, pl, x, b_dec, ws);
+    g.ab_fmt = pl.ab_fmt;
+    g.K = x->cols;
+    g.b_mn_major = pl.b_mn;
+    if (pl.w_direct) {
+        g.b = W->data;
+        g.b_pitch = pl.w_pitch;
+        return SF_OK;
+    }
+    const int st = run_repack(W, wp, pl.w_pitch, pl.b_mn, s);
+    if (st) return st;
+    g.b = wp;
+    g.b_pitch = pl.w_pitch;
+    return SF_OK;
+}
+
+// Behind a split-precision GEMM: when the split found an inf or NaN operand (the GEMM then
+// exited at once), the shifted fp32 x and the CUDA-core IEEE kernel compute the call; both
+// launches are no-ops otherwise.
+int run_emu_fallback(const EncodePlan &pl, const sf_matrix *x, const sf_matrix *W, const sf_vector *b_dec,
+                     uint8_t *ws, const EpilogueArgs &ep, const CsrArgs *csr, cudaStream_t s) {
+    const unsigned *flag = reinterpret_cast<const unsigned *>(ws + pl.flag_off);
+    float *xs32 = reinterpret_cast<float *>(ws + pl.xs32_off);
+    const int st = run_shift_convert(x, b_dec, SF_F32, xs32, pl.xs32_pitch, s, flag);
+    if (st) return st;
+    return encode_simt_f32(xs32, pl.xs32_pitch, static_cast<const float *>(W->data), W->stride_row, W->stride_col,
+                           x->rows, W->cols, x->cols, ep, s, csr, flag);
 }
 
 }  // namespace
@@ -464,12 +574,6 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    void *xs = ws;
-    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
-    if (!pl.fused_x) {
-        st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
-        if (st) return st;
-    }
 
     EpilogueArgs ep{};
     ep.b_enc = b_enc->data;
@@ -491,27 +595,18 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
                      : 0;
     ep.row_nnz = row_nnz;
 
-    if (!pl.tensor_cores)
-        return encode_simt_f32(static_cast<const float *>(xs), pl.a_pitch, static_cast<const float *>(W_enc->data),
-                               W_enc->stride_row, W_enc->stride_col, M, N, K, ep, s);
-
-    GemmOperands g{};
-    set_a_operand(g, pl, x, b_dec, xs);
-    g.ab_fmt = pl.ab_fmt;
-    g.M = M;
-    g.N = N;
-    g.K = K;
-    g.b_mn_major = pl.b_mn;
-    if (pl.w_direct) {
-        g.b = W_enc->data;
-        g.b_pitch = pl.w_pitch;
-    } else {
-        st = run_repack(W_enc, wp, pl.w_pitch, pl.b_mn, s);
+    if (!pl.tensor_cores) {
+        st = run_shift_convert(x, b_dec, pl.mma_dtype, ws, pl.a_pitch, s);
         if (st) return st;
-        g.b = wp;
-        g.b_pitch = pl.w_pitch;
+        return encode_simt_f32(reinterpret_cast<const float *>(ws), pl.a_pitch,
+                               static_cast<const float *>(W_enc->data), W_enc->stride_row, W_enc->stride_col, M, N,
+                               K, ep, s);
     }
-    return encode_tc_dense(g, ep, variant, s);
+    GemmOperands g;
+    st = prepare_tc(pl, x, W_enc, b_dec, ws, s, g);
+    if (!st) st = encode_tc_dense(g, ep, variant, s);
+    if (st || !pl.emulate) return st;
+    return run_emu_fallback(pl, x, W_enc, b_dec, ws, ep, nullptr, s);
 }
 
 int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc, const sf_vector *b_dec,
@@ -547,46 +642,6 @@ int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vec
     if (!aligned16(workspace)) return set_error(SF_ERR_WORKSPACE, "workspace must be 16-byte aligned");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    void *xs = ws;
-    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
-    if (!pl.fused_x) {
-        st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
-        if (st) return st;
-    }
-    if (!pl.tensor_cores) {
-        // IEEE fp32: the CUDA-core encoder with the same CSR staging epilogue
-        EpilogueArgs ep{};
-        ep.b_enc = b_enc->data;
-        ep.b_enc_dtype = b_enc->dtype;
-        ep.b_enc_stride = b_enc->stride;
-        if (threshold && threshold->data) {
-            ep.thr = threshold->data;
-            ep.thr_dtype = threshold->dtype;
-            ep.thr_stride = threshold->stride;
-        }
-        ep.activation = activation;
-        ep.out_dtype = values_dtype;
-        ep.row_nnz = row_nnz;
-        CsrArgs csr{tile_counts, tile_offsets, stage_indices, stage_values, state, (unsigned)stage_capacity};
-        return encode_simt_f32(static_cast<const float *>(xs), pl.a_pitch, static_cast<const float *>(W_enc->data),
-                               W_enc->stride_row, W_enc->stride_col, M, N, K, ep, s, &csr);
-    }
-    GemmOperands g{};
-    set_a_operand(g, pl, x, b_dec, xs);
-    g.ab_fmt = pl.ab_fmt;
-    g.M = M;
-    g.N = N;
-    g.K = K;
-    g.b_mn_major = pl.b_mn;
-    if (pl.w_direct) {
-        g.b = W_enc->data;
-        g.b_pitch = pl.w_pitch;
-    } else {
-        st = run_repack(W_enc, wp, pl.w_pitch, pl.b_mn, s);
-        if (st) return st;
-        g.b = wp;
-        g.b_pitch = pl.w_pitch;
-    }
     EpilogueArgs ep{};
     ep.b_enc = b_enc->data;
     ep.b_enc_dtype = b_enc->dtype;
@@ -600,7 +655,19 @@ int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vec
     ep.out_dtype = values_dtype;
     ep.row_nnz = row_nnz;
     CsrArgs csr{tile_counts, tile_offsets, stage_indices, stage_values, state, (unsigned)stage_capacity};
-    return encode_tc_csr(g, ep, csr, s);
+    if (!pl.tensor_cores) {
+        // the CUDA-core IEEE encoder with the same CSR staging epilogue
+        st = run_shift_convert(x, b_dec, pl.mma_dtype, ws, pl.a_pitch, s);
+        if (st) return st;
+        return encode_simt_f32(reinterpret_cast<const float *>(ws), pl.a_pitch,
+                               static_cast<const float *>(W_enc->data), W_enc->stride_row, W_enc->stride_col, M, N,
+                               K, ep, s, &csr);
+    }
+    GemmOperands g;
+    st = prepare_tc(pl, x, W_enc, b_dec, ws, s, g);
+    if (!st) st = encode_tc_csr(g, ep, csr, s);
+    if (st || !pl.emulate) return st;
+    return run_emu_fallback(pl, x, W_enc, b_dec, ws, ep, &csr, s);
 }
 
 int sf_csr_place(const int32_t *tile_counts, const int32_t *tile_offsets, int64_t M, int64_t d_sae,
@@ -803,30 +870,10 @@ int sf_topk_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *
     if (st) return st;
     const int chunks = topk_chunks(M, N);
     const size_t cand_off = (size_t)round_up((int64_t)plan_workspace(pl), 256);
-    void *xs = ws;
-    void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
     auto *cand = reinterpret_cast<unsigned long long *>(ws + cand_off);
-
-    if (!pl.fused_x) {
-        st = run_shift_convert(x, b_dec, pl.mma_dtype, xs, pl.a_pitch, s);
-        if (st) return st;
-    }
-    GemmOperands g{};
-    set_a_operand(g, pl, x, b_dec, xs);
-    g.ab_fmt = pl.ab_fmt;
-    g.M = M;
-    g.N = N;
-    g.K = K;
-    g.b_mn_major = pl.b_mn;
-    if (pl.w_direct) {
-        g.b = W_enc->data;
-        g.b_pitch = pl.w_pitch;
-    } else {
-        st = run_repack(W_enc, wp, pl.w_pitch, pl.b_mn, s);
-        if (st) return st;
-        g.b = wp;
-        g.b_pitch = pl.w_pitch;
-    }
+    GemmOperands g;
+    st = prepare_tc(pl, x, W_enc, b_dec, ws, s, g);
+    if (st) return st;
     TopkArgs tk{};
     tk.b_enc = b_enc->data;
     tk.b_enc_dtype = b_enc->dtype;

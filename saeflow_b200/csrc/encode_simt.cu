@@ -134,10 +134,11 @@ __device__ __forceinline__ void simt_csr_epilogue(const float (&o)[8][16], int m
     }
 }
 
+// One 128 x (64 NF) output tile at (m0, n0).
 template <int NF, bool CSR>
-__global__ void __launch_bounds__(SB_T, 1)
-    encode_simt_kernel(const float *__restrict__ xs, int64_t ldx, const float *__restrict__ W, int64_t swk,
-                       int64_t swn, int M, int N, int K, EpilogueArgs ep, int w_vec, CsrArgs csr, int n_tiles) {
+__device__ __forceinline__ void simt_tile(const float *__restrict__ xs, int64_t ldx, const float *__restrict__ W,
+                                          int64_t swk, int64_t swn, int M, int N, int K, const EpilogueArgs &ep,
+                                          int w_vec, const CsrArgs &csr, int n_tiles, int m0, int n0) {
     constexpr int SB_N = 64 * NF;
     constexpr int BQ = NF / 2;  // float4 loads of the B tile per thread per K step
     __shared__ __align__(16) float As[2][SB_K][SB_M + 4];
@@ -146,7 +147,6 @@ __global__ void __launch_bounds__(SB_T, 1)
 
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * SB_M, n0 = blockIdx.x * SB_N;
 
     for (int j = tid; j < SB_N; j += SB_T) {
         const int col = n0 + j;
@@ -286,26 +286,56 @@ __global__ void __launch_bounds__(SB_T, 1)
     }  // dense epilogue
 }
 
+// Tiles in row-major order over (m-tile, n-tile), n fastest. LOOP = false: one tile per CTA
+// (the grid covers them all). LOOP = true: the gated launch, one CTA per SM looping over the
+// tiles, so that skipping it costs one short wave (the loop costs the CSR variant a few
+// spilled registers, which only the rare non-finite fallback pays).
+template <int NF, bool CSR, bool LOOP>
+__global__ void __launch_bounds__(SB_T, 1)
+    encode_simt_kernel(const float *__restrict__ xs, int64_t ldx, const float *__restrict__ W, int64_t swk,
+                       int64_t swn, int M, int N, int K, EpilogueArgs ep, int w_vec, CsrArgs csr, int n_tiles,
+                       int tiles_n, int64_t tiles, const unsigned *gate) {
+    if (gate != nullptr && *reinterpret_cast<const volatile unsigned *>(gate) == 0u) return;
+    if constexpr (LOOP) {
+        for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const int m0 = (int)(t / tiles_n) * SB_M, n0 = (int)(t % tiles_n) * (64 * NF);
+            simt_tile<NF, CSR>(xs, ldx, W, swk, swn, M, N, K, ep, w_vec, csr, n_tiles, m0, n0);
+            __syncthreads();  // the next tile reuses the shared operand and bias arrays
+        }
+    } else {  // grid (n-tiles, m-tiles)
+        simt_tile<NF, CSR>(xs, ldx, W, swk, swn, M, N, K, ep, w_vec, csr, n_tiles, blockIdx.y * SB_M,
+                           blockIdx.x * (64 * NF));
+    }
+}
+
 }  // namespace
 
 int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
-                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream, const CsrArgs *csr) {
+                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream, const CsrArgs *csr,
+                    const unsigned *gate) {
     const bool wide = N >= 256 || csr != nullptr;  // CSR staging needs whole 256-column tiles
     const int64_t sb_n = wide ? 256 : 128;
-    if ((N + sb_n - 1) / sb_n > 2147483647ll || (M + SB_M - 1) / SB_M > 65535)
-        return set_error(SF_ERR_UNSUPPORTED, "SIMT encode grid too large (M=%lld N=%lld)", (long long)M, (long long)N);
+    const int64_t tiles_n = (N + sb_n - 1) / sb_n, tiles_m = (M + SB_M - 1) / SB_M, tiles = tiles_n * tiles_m;
     const int w_vec = (swn == 1 && (swk % 4) == 0 && (reinterpret_cast<uintptr_t>(W) & 15u) == 0) ? 1 : 0;
-    dim3 grid((unsigned)((N + sb_n - 1) / sb_n), (unsigned)((M + SB_M - 1) / SB_M));
+    // One CTA per tile on a (n-tiles, m-tiles) grid; a gated launch (a no-op unless the split
+    // found a non-finite operand) takes one CTA per SM looping over the tiles, so that
+    // skipping it costs one short wave.
+    const bool loop = gate != nullptr && tiles > num_sms();
+    if (!loop && (tiles_n > 2147483647ll || tiles_m > 65535))
+        return set_error(SF_ERR_UNSUPPORTED, "SIMT encode grid too large (M=%lld N=%lld)", (long long)M, (long long)N);
+    const dim3 grid = loop ? dim3((unsigned)num_sms()) : dim3((unsigned)tiles_n, (unsigned)tiles_m);
     const int n_tiles = (int)((N + kCsrTile - 1) / kCsrTile);
+    const CsrArgs c = csr ? *csr : CsrArgs{};
+    auto launch = [&](auto kern) {
+        kern<<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep, w_vec, c, n_tiles,
+                                        (int)tiles_n, tiles, gate);
+    };
     if (csr)
-        encode_simt_kernel<4, true><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K, ep,
-                                                               w_vec, *csr, n_tiles);
+        loop ? launch(encode_simt_kernel<4, true, true>) : launch(encode_simt_kernel<4, true, false>);
     else if (wide)
-        encode_simt_kernel<4, false><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K,
-                                                                ep, w_vec, CsrArgs{}, n_tiles);
+        loop ? launch(encode_simt_kernel<4, false, true>) : launch(encode_simt_kernel<4, false, false>);
     else
-        encode_simt_kernel<2, false><<<grid, SB_T, 0, stream>>>(xs, xs_pitch, W, swk, swn, (int)M, (int)N, (int)K,
-                                                                ep, w_vec, CsrArgs{}, n_tiles);
+        loop ? launch(encode_simt_kernel<2, false, true>) : launch(encode_simt_kernel<2, false, false>);
     return check_cuda(cudaGetLastError(), "encode_simt launch");
 }
 

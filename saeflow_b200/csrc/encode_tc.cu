@@ -102,7 +102,31 @@ struct TcParams {
     int bdec_dtype;
     int64_t bdec_stride;
     int bdec_mode;
+    // split-operand K schedule and the early-exit flag (see GemmOperands)
+    int seg_kb;
+    uint32_t seg_a, seg_b;
+    const unsigned *skip;
 };
+
+// TMA K coordinates of K block kb in A and in B. Plain GEMM: both kb * bk. Split-operand
+// schedule: block kb lies in segment pair s = kb / seg_kb, whose A and B segments come from
+// the seg_a / seg_b nibbles.
+__device__ __forceinline__ void k_coords(const TcParams &p, int kb, int bk, int &ka, int &kw) {
+    if (p.seg_kb == 0) {
+        ka = kw = kb * bk;
+        return;
+    }
+    const int s = kb / p.seg_kb;
+    const int off = (kb - s * p.seg_kb) * bk;
+    const int span = p.seg_kb * bk;
+    ka = (int)((p.seg_a >> (4 * s)) & 15u) * span + off;
+    kw = (int)((p.seg_b >> (4 * s)) & 15u) * span + off;
+}
+
+// The split-precision encode's non-finite fallback: set before launch by the operand split.
+__device__ __forceinline__ bool skip_launch(const TcParams &p) {
+    return p.skip != nullptr && *reinterpret_cast<const volatile unsigned *>(p.skip) != 0u;
+}
 
 // The staged bias / cut arrays are read as float4: they must start on 16-byte boundaries.
 struct __align__(16) TcShared {
@@ -664,6 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    if (skip_launch(p)) return;  // before any barrier or TMEM allocation
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -714,14 +739,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
                         uint8_t *a_dst = sA + stage * kTileABytes;
                         uint8_t *b_dst = sB + stage * kTileBBytes;
-                        tma_load_2d(a_dst, &tmA, &sh->full[stage], kb * BK, un.m_blk * kBM, pol_x);
+                        int ka, kw;
+                        k_coords(p, kb, BK, ka, kw);
+                        tma_load_2d(a_dst, &tmA, &sh->full[stage], ka, un.m_blk * kBM, pol_x);
                         if (B_MN) {
 #pragma unroll
                             for (int j = 0; j < kBN / MN_BOX; ++j)
                                 tma_load_2d(b_dst + j * MN_BOX_BYTES, &tmB, &sh->full[stage],
-                                            n_blk * kBN + j * MN_BOX, kb * BK, pol_w);
+                                            n_blk * kBN + j * MN_BOX, kw, pol_w);
                         } else {
-                            tma_load_2d(b_dst, &tmB, &sh->full[stage], kb * BK, n_blk * kBN, pol_w);
+                            tma_load_2d(b_dst, &tmB, &sh->full[stage], kw, n_blk * kBN, pol_w);
                         }
                         if (++stage == STAGES) {
                             stage = 0;
@@ -878,6 +905,8 @@ __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kCon
     const bool leader = rank == 0;
     const int pair = (int)cluster_id_x();
     const int npairs = (int)num_clusters_x();
+    // Both CTAs of the pair read the same flag, so both leave before any cluster barrier.
+    if (skip_launch(p)) return;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -944,8 +973,10 @@ __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kCon
                             armed |= 1u << stage;
                             armed_parity = (armed_parity & ~(1u << stage)) | (phase << stage);
                         }
+                        int ka, kw;
+                        k_coords(p, kb, BK, ka, kw);
                         if (!CONV_A)
-                            tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_leader, kb * BK,
+                            tma_load_2d_pair(sA + stage * A_BYTES, &tmA, full_leader, ka,
                                              un.m_blk * 256 + (int)rank * 128, pol_x);
                         uint8_t *b_dst = sB + stage * B_BYTES;
                         const int n0 = n_blk * kBN + (int)rank * HALF_N;
@@ -953,9 +984,9 @@ __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kCon
 #pragma unroll
                             for (int j = 0; j < HALF_N / MN_BOX; ++j)
                                 tma_load_2d_pair(b_dst + j * MN_BOX_BYTES, &tmB, full_leader, n0 + j * MN_BOX,
-                                                 kb * BK, pol_w);
+                                                 kw, pol_w);
                         } else {
-                            tma_load_2d_pair(b_dst, &tmB, full_leader, kb * BK, n0, pol_w);
+                            tma_load_2d_pair(b_dst, &tmB, full_leader, kw, n0, pol_w);
                         }
                         if (++stage == STAGES) {
                             stage = 0;
@@ -1268,6 +1299,11 @@ void fill_common(TcParams &p, const GemmOperands &g, bool pair, unsigned *err) {
     p.num_m_tiles = (int)((g.M + p.bm - 1) / p.bm);
     p.num_n_tiles = (int)((g.N + kBN - 1) / kBN);
     p.num_kb = (int)((g.K + (128 / es) - 1) / (128 / es));
+    p.seg_kb = g.seg_kb;
+    p.seg_a = g.seg_a;
+    p.seg_b = g.seg_b;
+    p.skip = g.skip;
+    if (g.seg_kb > 0) p.num_kb = kEmuPairs * g.seg_kb;
     p.err = err;
     p.xa = g.a;
     p.xa_pitch = g.a_pitch;

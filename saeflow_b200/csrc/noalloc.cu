@@ -52,6 +52,12 @@ SF_API int sf_fused_encode_noalloc(const sf_matrix *x, const sf_matrix *W_enc, c
                                    const sf_vector *b_dec, const sf_vector *threshold, int activation,
                                    const sf_matrix *out, int32_t *row_nnz, int allow_tf32, int variant,
                                    sf_stream stream) {
+    // IEEE fp32 products (fp32 x and W_enc, TF32 not allowed) run split-precision on the
+    // tensor cores by default, and the split copy of W_enc (three bf16 parts) outgrows the
+    // static scratch for any real SAE: here the CUDA-core IEEE kernel, which needs only the
+    // shifted x, serves those calls.
+    const bool ieee = x && W_enc && x->dtype == SF_F32 && W_enc->dtype == SF_F32 && !allow_tf32;
+    if (ieee && variant == SF_VARIANT_AUTO) variant = SF_VARIANT_SIMT;
     size_t need = 0;
     int st = sf_fused_encode_workspace(x, W_enc, allow_tf32, variant, &need);
     if (st) return st;
@@ -63,6 +69,13 @@ SF_API int sf_fused_encode_noalloc(const sf_matrix *x, const sf_matrix *W_enc, c
         size_t w_part = 0;
         st = sf_fused_encode_workspace(&x0, W_enc, allow_tf32, variant, &w_part);
         if (st) return st;
+        if (w_part + 256 > kScratchBytes && ieee)
+            return sf::set_error(SF_ERR_WORKSPACE,
+                                 "sf_fused_encode_noalloc: IEEE fp32 on the tensor cores needs a split copy of "
+                                 "W_enc (%zu bytes) that does not fit the %zu-byte static scratch. Pass variant "
+                                 "SF_VARIANT_AUTO or SF_VARIANT_SIMT (the CUDA-core IEEE kernel), or call "
+                                 "sf_fused_encode with a workspace.",
+                                 w_part, kScratchBytes);
         if (w_part + 256 > kScratchBytes)
             return sf::set_error(SF_ERR_WORKSPACE,
                                  "sf_fused_encode_noalloc: W_enc is in a layout the tensor-core kernel cannot read "

@@ -1,6 +1,7 @@
 // Host-side interfaces between the saeflow_b200 translation units.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -28,7 +29,47 @@ struct GemmOperands {
     int bdec_dtype;
     int64_t bdec_stride;
     int bdec_mode;
+    // Split-operand K schedule (IEEE-grade fp32 on bf16 tensor cores, emulate.cu): when
+    // seg_kb > 0, A and B each hold 3 segments of seg_kb K blocks and the kernel runs
+    // kEmuPairs segment pairs, pair s reading A segment (seg_a >> 4s) & 15 against B segment
+    // (seg_b >> 4s) & 15. K is then the extent of the stored segments (3 seg_kb blocks).
+    int seg_kb;
+    uint32_t seg_a, seg_b;
+    // When non-null and nonzero at launch, the kernel exits without touching any output.
+    const unsigned *skip;
 };
+
+// Operands of the split-precision fp32 encode (emulate.cu): x (fp32, any strides) minus
+// b_dec into a = [x0 | x1 | x2] ([M, 3 kp] bf16), W_enc (fp32 [K, N], any strides) into
+// b = [W0 ; W1 ; W2] ([3 kp, N] bf16, row pitch b_pitch); *flag = 1 if any operand is not
+// finite.
+struct EmuOperands {
+    const float *x;
+    int64_t M, K, sxm, sxk;
+    const void *b_dec;
+    int b_dtype;
+    int64_t b_stride;
+    const float *W;
+    int64_t N, swk, swn;
+    __nv_bfloat16 *a;
+    __nv_bfloat16 *b;
+    int64_t kp, b_pitch;
+    unsigned *flag;
+};
+constexpr int kEmuKBlock = 64;  // bf16 elements per GEMM K block: the segment padding
+constexpr int kEmuPairs = 6;
+// (a segment, b segment) pairs, smallest products first: (x2,W0) (x1,W1) (x0,W2) (x1,W0) (x0,W1) (x0,W0)
+constexpr uint32_t kEmuSegA = 0x001012u;  // nibble s = A segment of pair s
+constexpr uint32_t kEmuSegB = 0x010210u;  // nibble s = B segment of pair s
+int emu_split_operands(const EmuOperands &e, cudaStream_t s);
+// Largest d_in the AUTO variant sends to the split-precision route. Its partial products are
+// exact, but the tensor cores round the running fp32 sum once per 16-product MMA, toward
+// zero, so the error of the large (x0, W0) term grows with d_in / 16 (a bias, not a random
+// walk): measured on B200 against float64, max |error| 7.8e-6 at d_in 768 (the CUDA-core
+// IEEE kernel: 7.1e-6), within the fp32 contract (rtol 1e-5, atol 1e-5) at 2304, 89 of
+// 51200 features outside it at 4096 (worst 1.6e-5). Up to 1024 the bound d_in/16 * 2^-24
+// (3.8e-6 relative) leaves a 2.6x margin; beyond, AUTO runs the CUDA-core kernel.
+constexpr int64_t kEmuMaxAutoK = 1024;
 
 // 1: the CTA-pair kernel for 16-bit operands builds its A tiles with converter warps that
 // read x itself and subtract b_dec on the way (no shifted copy of x in HBM, no shift pass).
@@ -87,7 +128,10 @@ constexpr int kTopkMaxK = 112;  // shared-memory bound of the fused top-k lists 
 
 // IEEE fp32 encoder on the CUDA cores: dense output (csr == nullptr) or the CSR staging of
 // encode_tc_csr (same tile counts, offsets and column-ordered runs).
+// A non-null `gate` makes the launch a no-op unless *gate is nonzero (the non-finite-operand
+// fallback of the split-precision encode).
 int encode_simt_f32(const float *xs, int64_t xs_pitch, const float *W, int64_t swk, int64_t swn, int64_t M,
-                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream, const CsrArgs *csr = nullptr);
+                    int64_t N, int64_t K, const EpilogueArgs &ep, cudaStream_t stream, const CsrArgs *csr = nullptr,
+                    const unsigned *gate = nullptr);
 
 }  // namespace sf

@@ -48,12 +48,25 @@ def _variant(config) -> int:
     return _VARIANTS[v]
 
 
+SPLIT_PRECISION_MAX_D_IN = 1024  # kEmuMaxAutoK of the library: the "auto" limit of the split route
+
+
 def _uses_tensor_cores(x, W_enc, allow_tf32, variant) -> bool:
-    if variant in (_abi.SF_VARIANT_TCGEN05, _abi.SF_VARIANT_TCGEN05_SINGLE):
-        return True
+    """Every kernel choice but "simt" runs on the tensor cores, except IEEE fp32 under "auto"
+    above SPLIT_PRECISION_MAX_D_IN, whose split-precision error would outgrow the fp32
+    tolerance (see _split_precision)."""
     if variant == _abi.SF_VARIANT_SIMT:
         return False
-    return W_enc.dtype != torch.float32 or allow_tf32 or x.dtype != torch.float32
+    if variant == _abi.SF_VARIANT_AUTO and _split_precision(x, W_enc, allow_tf32):
+        return x.shape[1] <= SPLIT_PRECISION_MAX_D_IN
+    return True
+
+
+def _split_precision(x, W_enc, allow_tf32) -> bool:
+    """fp32 x and W_enc with TF32 not allowed: the reference's IEEE products
+    (encode.py:118-120), computed on the bf16 tensor cores from three-part splits of both
+    operands, smallest partial products first, to fp32-class accuracy."""
+    return W_enc.dtype == torch.float32 and x.dtype == torch.float32 and not allow_tf32
 
 
 def fused_encode(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *,
@@ -105,6 +118,8 @@ def fused_encode(x, W_enc, b_enc, b_dec, threshold=None, activation="relu", *,
         _last_config = dict(TCGEN05_PAIR_CONFIG)
     else:
         _last_config = dict(TCGEN05_CONFIG)
+    if _split_precision(x, W_enc, allow_tf32) and _last_config["variant"] != "simt":
+        _last_config["operands"] = "bf16 x3 split, 6 partial products"
     return out
 
 

@@ -116,15 +116,24 @@ def _even_split(n, cap):
     return [n // k + (1 if i < n % k else 0) for i in range(k)]
 
 
+# Smallest batch (rows) forward_host splits although it fits one chunk.
+SMALL_SPLIT_ROWS = 2048
+
+
 def _chunk_plan(M, C):
     """Row counts of forward_host's chunks (at most C each): quarter and half chunks at both
     ends, full chunks between. Only the first chunk's copy in and the last chunk's copy out
     are exposed, and every chunk pays a fixed cost (the weights are streamed again, and the
     scans run again: ~0.1 ms at config 2), so the plan keeps both ends short with few chunks.
     Measured on B200 at config 2 (16384 rows, C = 8192): 4.66 ms against 3.94 ms with the
-    batch already on the device; plans with more or with smaller end chunks were slower."""
+    batch already on the device; plans with more or with smaller end chunks were slower.
+    A batch of one chunk or less still splits quarter / half / quarter from SMALL_SPLIT_ROWS
+    rows up, so that its copies overlap the compute too."""
     if M <= C:
-        return [M]
+        if M < SMALL_SPLIT_ROWS:
+            return [M]
+        q = M // 4
+        return [q, M - 2 * q, q]
     ramp = [max(1, C // 4), max(1, C // 2)]
     mid = M - 2 * sum(ramp)
     if mid <= 0:

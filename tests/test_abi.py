@@ -65,6 +65,19 @@ def test_workspace_sizes():
     # the CUDA-core kernel is fp32 only
     assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 2, ctypes.byref(need)) == \
         _abi.SF_ERR_UNSUPPORTED
+    # IEEE fp32 (config 1 shapes): the split x [M, 3 kp] bf16, the fallback's fp32 shifted x, a
+    # 256-byte flag, the split W_enc [3 kp, N] bf16 (kp = d_in rounded up to 64); the CUDA-core
+    # kernel needs only the fp32 shifted x
+    x = _abi.SfMatrix(16, 0, 0, 4096, 768, 768, 1)
+    W = _abi.SfMatrix(16, 0, 0, 768, 16384, 16384, 1)
+    assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
+    assert need.value == 4096 * 3 * 768 * 2 + 4096 * 768 * 4 + 256 + 3 * 768 * 16384 * 2
+    assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 2, ctypes.byref(need)) == 0
+    assert need.value == 4096 * 768 * 4
+    x = _abi.SfMatrix(16, 0, 0, 10, 100, 100, 1)  # d_in 100 -> kp 128; d_sae 129 -> pitch 136
+    W = _abi.SfMatrix(16, 0, 0, 100, 129, 129, 1)
+    assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
+    assert need.value == 7680 + 4352 + 256 + 3 * 128 * 136 * 2  # 10x384x2, and 10x104x4 rounded up to 256
 
 
 def test_ops_refuse_cpu_tensors():

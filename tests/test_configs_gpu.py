@@ -92,14 +92,21 @@ def check_decoded_rows(sae, out, csr_rows, rows):
     contract.assert_values_close(out[rows].cpu().float(), want.float(), sae.W_dec.dtype, what="decoded rows")
 
 
-def test_cfg1_relu_fp32_ieee_full_size():
+@pytest.mark.parametrize("variant", ["auto", "simt"])
+def test_cfg1_relu_fp32_ieee_full_size(variant):
+    """Config 1 under the fp32 contract (rtol 1e-5) on both IEEE-product routes: the default
+    split-precision tensor-core GEMM and the CUDA-core kernel."""
     dev = torch.device("cuda")
     sae = bench.make_sae(1, dev)
     x = bench.make_tokens(1, 0, dev)
     T = x.shape[0]
     rn = torch.zeros(T, dtype=torch.int32, device=dev)
-    f = fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, row_nnz=rn)
-    assert best_config()["variant"] == "simt"  # IEEE fp32 products, not TF32
+    f = fused_encode(x, sae.W_enc, sae.b_enc, sae.b_dec, row_nnz=rn, config={"variant": variant})
+    cfg = best_config()
+    if variant == "simt":
+        assert cfg["variant"] == "simt"
+    else:  # IEEE products from split operands on the tensor cores, not TF32
+        assert cfg["variant"] == "tcgen05" and "split" in cfg["operands"]
     assert torch.equal(rn, torch.count_nonzero(f, dim=1).int())
     csr = dense_to_csr(f, rn)
     ref = f.to_sparse_csr()
@@ -107,13 +114,13 @@ def test_cfg1_relu_fp32_ieee_full_size():
     assert torch.equal(bits(csr[2]), bits(ref.values()))
     l0 = csr[1].numel() / T
     assert 50 < l0 < 80, f"L0 {l0}"  # the config's b_enc = -2.66 gives L0 ~ 64
-    out = saeflow_b200.forward(sae, x)
-    assert torch.equal(bits(out), bits(sparse_decode(*csr, sae.W_dec, sae.b_dec)))
-
     rows = sample_rows(T)
     clean = check_encoded_rows(sae, x, f[rows], csr, rows)
     assert torch.equal(rn.cpu()[rows][clean], torch.count_nonzero(f[rows], dim=1).int().cpu()[clean])
-    check_decoded_rows(sae, out, sub_csr(csr, rows), rows)
+    if variant == "auto":  # forward encodes straight to CSR with the same arithmetic
+        out = saeflow_b200.forward(sae, x)
+        assert torch.equal(bits(out), bits(sparse_decode(*csr, sae.W_dec, sae.b_dec)))
+        check_decoded_rows(sae, out, sub_csr(csr, rows), rows)
 
 
 def test_cfg2_jumprelu_bf16_full_size():

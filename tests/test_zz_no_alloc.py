@@ -114,3 +114,40 @@ def test_noalloc_encode_rejects_a_weight_layout_it_would_have_to_copy():
     assert b"layout" in msg and b"column-major" in msg
     torch.cuda.synchronize()
     assert int(out.abs().sum()) == 0  # nothing ran
+
+
+def test_noalloc_ieee_fp32_runs_the_cuda_core_kernel():
+    """fp32 x and W_enc with TF32 off: the allocating call splits W_enc into bf16 parts for
+    the tensor cores, a copy the static scratch cannot hold, so the no-alloc call runs the
+    CUDA-core IEEE kernel (scratch: the shifted x), identical to the allocating call pinned
+    to that kernel."""
+    lib = _abi.load()
+    M, K, N = 700, 256, 2048
+    g = torch.Generator(device="cuda").manual_seed(15)
+    x = torch.randn(M, K, generator=g, device="cuda")
+    W = torch.randn(K, N, generator=g, device="cuda") / 16
+    b_enc, b_dec = torch.full((N,), -0.5, device="cuda"), torch.randn(K, generator=g, device="cuda") * 0.1
+    xm, wm, be, bd = _abi.matrix(x, "x"), _abi.matrix(W, "W_enc"), _abi.vector(b_enc, "b_enc"), _abi.vector(b_dec, "b_dec")
+    outs = []
+    for noalloc in (False, True):
+        out = torch.full((M, N), float("nan"), device="cuda")
+        nnz = torch.zeros(M, device="cuda", dtype=torch.int32)
+        om = _abi.matrix(out, "out")
+        if noalloc:
+            st = lib.sf_fused_encode_noalloc(ctypes.byref(xm), ctypes.byref(wm), ctypes.byref(be), ctypes.byref(bd),
+                                             None, _abi.SF_ACT_RELU, ctypes.byref(om), nnz.data_ptr(), 0, 0,
+                                             _abi.stream_of(x.device))
+        else:
+            need = ctypes.c_size_t(0)
+            _abi.check(lib.sf_fused_encode_workspace(ctypes.byref(xm), ctypes.byref(wm), 0, _abi.SF_VARIANT_SIMT,
+                                                     ctypes.byref(need)))
+            ws = torch.empty(need.value, device="cuda", dtype=torch.uint8)
+            st = lib.sf_fused_encode(ctypes.byref(xm), ctypes.byref(wm), ctypes.byref(be), ctypes.byref(bd), None,
+                                     _abi.SF_ACT_RELU, ctypes.byref(om), nnz.data_ptr(), 0, _abi.SF_VARIANT_SIMT,
+                                     ws.data_ptr(), ws.numel(), _abi.stream_of(x.device))
+        _abi.check(st)
+        torch.cuda.synchronize()
+        outs.append((out, nnz))
+    assert torch.equal(outs[0][0].view(torch.int32), outs[1][0].view(torch.int32))
+    assert torch.equal(outs[0][1], outs[1][1])
+    assert _abi.device_error() == 0
