@@ -1420,15 +1420,19 @@ constexpr double kTopkWaveEff = 0.94;
 #ifndef SF_TOPK_MIN_BUF
 #define SF_TOPK_MIN_BUF 24
 #endif
+#ifndef SF_TOPK_MAX_TPC
+#define SF_TOPK_MAX_TPC (1 << 30)
+#endif
 int topk_chunks(int64_t M, int64_t N) {
     const bool pair = M > kBM;
     const int bm = pair ? 256 : kBM;
     const int m_tiles = (int)((M + bm - 1) / bm);
     const int n_tiles = (int)((N + kBN - 1) / kBN);
     const int slots = pair ? std::max(1, num_sms() / 2) : num_sms();
-    int best = 1;
+    const int c_min = std::max(1, (n_tiles + SF_TOPK_MAX_TPC - 1) / SF_TOPK_MAX_TPC);
+    int best = c_min;
     double best_eff = -1.0;
-    for (int c = 1; c <= std::min(n_tiles, 32); ++c) {
+    for (int c = c_min; c <= std::min(n_tiles, std::max(32, c_min)); ++c) {
         const int tpc = (n_tiles + c - 1) / c;
         const int chunks = (n_tiles + tpc - 1) / tpc;
         const long units = (long)m_tiles * chunks;

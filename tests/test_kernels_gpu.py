@@ -435,6 +435,40 @@ def test_forward_host_matches_forward(activation, chunk, whole, monkeypatch):
     assert device_error() == 0
 
 
+@pytest.mark.parametrize("whole", [True, False])
+def test_forward_host_async_pipelined_calls(whole, monkeypatch):
+    """Three forward_host_async calls in flight at once, on different batches and outputs,
+    waited in reverse order: each equals forward_host of its own batch bit for bit. A call
+    whose CSR staging overflows is redone in wait() like forward_host's."""
+    from saeflow_b200 import forward_host, forward_host_async, ops
+
+    if not whole:
+        monkeypatch.setattr(ops, "WHOLE_BATCH_DEVICE_BYTES", 0)
+    sae = _sparse_sae(256, 4099, "jumprelu")
+    xs = [torch.randn(M, 256).to(torch.bfloat16).pin_memory() for M in (3000, 700, 2500)]
+    want = [forward_host(sae, x, chunk_tokens=1024) for x in xs]
+    outs = [torch.empty(x.shape[0], 256, dtype=torch.bfloat16).pin_memory() for x in xs]
+    pend = [forward_host_async(sae, x, o, chunk_tokens=1024) for x, o in zip(xs, outs)]
+    for p, o, w in reversed(list(zip(pend, outs, want))):
+        assert p.wait() is o
+        assert torch.equal(o.view(torch.int16), w.view(torch.int16))
+    assert pend[0].wait() is outs[0]  # a second wait returns the same output
+    # chunk_tokens=None: one launch per FORWARD_CHUNK_ROWS rows, as forward() on the device
+    for x in xs:
+        assert torch.equal(forward_host_async(sae, x, chunk_tokens=None).wait().view(torch.int16),
+                           ops.forward(sae, x.cuda()).cpu().view(torch.int16))
+    dense = make_sae(64, 600, "relu", torch.bfloat16).to("cuda")
+    dense.b_enc[:] = -5.0
+    dense.b_enc[:550] = 5.0  # > 512 active features per row: the default staging overflows
+    x = torch.randn(300, 64).to(torch.bfloat16)
+    got = forward_host_async(dense, x).wait()
+    rn = torch.zeros(300, device="cuda", dtype=torch.int32)
+    f = fused_encode(x.cuda(), dense.W_enc, dense.b_enc, dense.b_dec, row_nnz=rn)
+    ref = sparse_decode(*dense_to_csr(f, rn), dense.W_dec, dense.b_dec).cpu()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
+    assert device_error() == 0
+
+
 # ----------------------------------------------------------------------------- decode
 
 @pytest.mark.parametrize("shape", SHAPES)
