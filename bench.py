@@ -731,7 +731,7 @@ def cpu_dense_forward_row(ref, x, budget_s):
 
 
 def cpu_baseline(cfg_id, budget_s=10.0, sample_tokens=None):
-    cores = torch.get_num_threads()
+    cores = host_threads()
     ref, x = cpu_pipeline_setup(cfg_id, sample_tokens or (1024 if cfg_id != 1 else 4096))
     cpu_step(ref, x[:64])  # warm-up
     n, dt = time_cpu(lambda: cpu_step(ref, x), budget_s)
@@ -796,10 +796,19 @@ def run_reference_triton(args, device):
     }
 
 
+def host_threads():
+    """Every host thread this process may run on: torchrun sets OMP_NUM_THREADS=1 per rank, and
+    the CPU baselines (rank 0 alone) use the whole host."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
+    return n
+
+
 def run_reference(args):
     cfg_id = args.config
     c = CONFIGS[cfg_id]
     sample = args.cpu_tokens
+    host_threads()
     ref, x = cpu_pipeline_setup(cfg_id, sample)
     for _ in range(args.warmup):
         cpu_step(ref, x)
