@@ -77,6 +77,30 @@ def test_split_precision_within_fp32_contract(shape, layout):
     assert mx <= 4 * mx_s + 1e-7 and rms <= 3 * rms_s + 1e-8, (mx, rms, mx_s, rms_s)
 
 
+@pytest.mark.parametrize("x_layout", ["transposed", "sliced"])
+def test_split_precision_strided_x_and_b_dec(x_layout):
+    """x column-major (the split's scalar path) or a column slice of a wider matrix, b_dec a
+    strided fp16 view: same contract against the oracle, and the same values as contiguous
+    operands (the split sees the same fp32 differences)."""
+    M, d_in, d_sae = 333, 200, 1100
+    x, W, b_enc, b_dec = _operands(M, d_in, d_sae, seed=21)
+    if x_layout == "transposed":
+        xs = x.T.contiguous().T
+    else:
+        wide = torch.zeros(M, d_in + 5, device="cuda")
+        wide[:, 3:d_in + 3] = x
+        xs = wide[:, 3:d_in + 3]
+    bd16 = torch.zeros(2 * d_in, device="cuda", dtype=torch.float16)
+    bd16[::2] = b_dec.half()
+    bd = bd16[::2]
+    got = fused_encode(xs, W, b_enc, bd)
+    ref = fused_encode(x.contiguous(), W, b_enc, bd.contiguous())
+    assert torch.equal(got.view(torch.int32), ref.view(torch.int32))
+    want, _, pre = oracle.fused_encode(x.cpu(), W.cpu(), b_enc.cpu(), bd.cpu())
+    near = contract.near_cut(pre)
+    contract.assert_values_close(got.cpu()[~near], want[~near], torch.float32, what=x_layout)
+
+
 @pytest.mark.parametrize("d_in", [1025, 4096])
 def test_auto_keeps_wide_ieee_fp32_on_the_cuda_cores(d_in):
     """Above d_in 1024 the tensor cores' per-MMA rounding of the running sum would outgrow
