@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import re
 import math
 import os
 import sys
@@ -272,6 +273,18 @@ class ClockSampler:
         return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
                 "power_w_median": round(watts[len(watts) // 2], 1),
                 "samples": len(self.samples), "samples_under_load": len(loaded), "source": "nvml 10 ms"}
+
+
+def encode_errors(sae, x, f, rows=4096):
+    """Max and rms |error| of encoder output rows f[:rows] against the float64 product of the
+    same operands (activation applied to the float64 pre-activations)."""
+    xs = x[:rows].double() - sae.b_dec.double()
+    pre = xs @ sae.W_enc.double() + sae.b_enc.double()
+    want = pre.clamp_min(0)
+    if sae.activation == "jumprelu":
+        want = torch.where(pre > sae.threshold.double(), want, torch.zeros((), dtype=want.dtype, device=want.device))
+    d = (f[:rows].double() - want).abs()
+    return {"rows": int(d.shape[0]), "max_abs": float(d.max()), "rms": float(d.pow(2).mean().sqrt())}
 
 
 def l2_flush(buf):
@@ -660,6 +673,14 @@ def run_ours(args, rank, world, device):
         "clocks": clk.summary(),
         "wall_s_timed_region": round(wall, 3),
     }
+    if args.accuracy and cfg_id in (1, 2) and sharded is None:
+        acc = {"route": encode_errors(sae, x, fused_encode(x[:4096], sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold,
+                                                              sae.activation))}
+        if c["dtype"] == torch.float32:
+            acc["cuda_core_ieee"] = encode_errors(sae, x, fused_encode(x[:4096], sae.W_enc, sae.b_enc, sae.b_dec,
+                                                                      sae.threshold, sae.activation,
+                                                                      config={"variant": "simt"}))
+        line["accuracy"] = acc
     if not args.no_cpu_baseline and world == 1 and cfg_id != 5:
         line["cpu_baseline"] = cpu_baseline(cfg_id, budget_s=args.cpu_seconds)
     return line
@@ -781,7 +802,7 @@ def run_reference_triton(args, device):
     e_total = timed(lambda: out_host.copy_(saeflow.forward(sae, x_host.to(device, non_blocking=True)),
                                            non_blocking=True), args.steps)
     nbytes = T * c["d_in"] * x.element_size()
-    return {
+    line = {
         "metric": METRIC, "value": round(T * args.steps / (total / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -794,6 +815,10 @@ def run_reference_triton(args, device):
                 "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes},
         "clocks": clk.summary(),
     }
+    if args.accuracy and cfg_id in (1, 2):
+        f = saeflow.kernels.fused_encode(x[:4096], sae.W_enc, sae.b_enc, sae.b_dec, sae.threshold, sae.activation)
+        line["accuracy"] = {"route": encode_errors(sae, x, f)}
+    return line
 
 
 def host_threads():
@@ -859,7 +884,19 @@ def main(argv=None):
                     help="config 5 feature partition: tokens per all-reduced chunk")
     ap.add_argument("--route", choices=["csr", "dense"], default="csr",
                     help="csr: encode straight to CSR (default); dense: dense features + compaction")
+    ap.add_argument("--d-in", type=int, default=None, help="configs 1-4: override d_in (same distributions)")
+    ap.add_argument("--d-sae", type=int, default=None, help="configs 1-4: override d_sae (same distributions)")
+    ap.add_argument("--accuracy", action="store_true",
+                    help="fp32 configs: add the encoder's error against a float64 product (and, for this build, "
+                         "the CUDA-core IEEE kernel's) on up to 4096 rows")
     args = ap.parse_args(argv)
+    if args.d_in or args.d_sae:
+        if args.config == 5:
+            ap.error("--d-in / --d-sae apply to configs 1-4")
+        c = dict(CONFIGS[args.config])
+        c["d_in"], c["d_sae"] = args.d_in or c["d_in"], args.d_sae or c["d_sae"]
+        c["name"] = re.sub(r"d_in=\d+ d_sae=\d+", f"d_in={c['d_in']} d_sae={c['d_sae']}", c["name"])
+        CONFIGS[args.config] = c
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -55,7 +55,7 @@ enum sf_status {
 
 /* Encode variant selector (the `config=` kwarg of fused_encode).                  */
 enum sf_encode_variant {
-    SF_VARIANT_AUTO = 0,     /* tcgen05/TMEM kernel (IEEE fp32: split operands up to d_in 1024, CUDA cores above) */
+    SF_VARIANT_AUTO = 0,     /* the tcgen05/TMEM kernel for every dtype (IEEE fp32: split operands) */
     SF_VARIANT_TCGEN05 = 1,  /* force the tcgen05/TMEM kernel (CTA pairs when M > 128) */
     SF_VARIANT_SIMT = 2,     /* force the CUDA-core kernel (fp32 W_enc only)          */
     SF_VARIANT_TCGEN05_SINGLE = 3  /* tcgen05 kernel on single CTAs (128 x 256 tiles)  */
@@ -97,8 +97,10 @@ SF_API int sf_device_error(uint32_t *code);
  * Workspace bytes sf_fused_encode needs for these operands (the b_dec-shifted,
  * dtype-converted copy of x, plus a repacked W_enc when its layout cannot be read by
  * TMA; for IEEE fp32 on the tensor cores the three-part bf16 splits of the shifted x and of
- * W_enc, 6 d_in' bytes per row and 6 d_in' bytes per feature with d_in' = d_in rounded up
- * to 64, plus 4 d_in bytes per row for the non-finite fallback). Replaces the
+ * W_enc for one K range, 6 k' bytes per row and 6 k' bytes per feature with k' = the range
+ * (d_in up to 1024, else d_in split evenly into ranges of at most 1024) rounded up to 64,
+ * 4 d_in bytes per row for the non-finite fallback and, with more than one range, 4 bytes
+ * per (row, feature rounded up to 256) of fp32 partial sums). Replaces the
  * allocation-free Triton launch of saeflow/kernels/encode.py:115-139.
  */
 SF_API int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc, int allow_tf32,
@@ -117,11 +119,12 @@ SF_API int sf_fused_encode_workspace(const sf_matrix *x, const sf_matrix *W_enc,
  *            too these run on the bf16 tensor cores by default: both operands split into
  *            three bf16 parts (Henry, Tang & Heinecke, ARITH 2019), the six partial products
  *            above 2^-23 summed smallest first in the fp32 accumulator. The tensor cores
- *            round that sum toward zero once per 16 products, an error growing with d_in:
- *            at d_in 768 it matches fp32 FMA chains, so SF_VARIANT_AUTO takes this route up
- *            to d_in 1024 and the CUDA-core IEEE kernel beyond (SF_VARIANT_TCGEN05 forces the
- *            split route, SF_VARIANT_SIMT the CUDA-core kernel). An inf or NaN operand makes
- *            the call run on the CUDA-core kernel instead (decided on the device, no sync).
+ *            round that sum toward zero once per 16 products, an error growing with the K
+ *            range, so d_in runs in ranges of at most 1024 whose sums are added in fp32
+ *            round-to-nearest: errors of the order of fp32 FMA chains (measured at d_in 768
+ *            and 2304). SF_VARIANT_SIMT pins the CUDA-core IEEE kernel. An inf or NaN operand
+ *            makes the call run on the CUDA-core kernel instead (decided on the device, no
+ *            sync).
  */
 SF_API int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc,
                     const sf_vector *b_dec, const sf_vector *threshold, int activation,

@@ -256,12 +256,15 @@ struct EncodePlan {
     int64_t w_pitch; // pitch of W_enc as TMA sees it (elements)
     size_t xs_bytes, wp_bytes;
     bool fused_x;    // the CTA-pair kernel's converter warps read x itself and shift it (no copy)
-    // IEEE fp32 on the bf16 tensor cores (emulate.cu). Workspace: the split x [M, 3 kp] bf16,
-    // then (at xs32_off) the fp32 shifted x of the non-finite fallback, then the fallback
-    // flag (at flag_off), then the split W_enc [3 kp, w_pitch] bf16.
+    // IEEE fp32 on the bf16 tensor cores (emulate.cu), in nkc K ranges of kc columns of x
+    // (the last one shorter). Workspace: the split x of one range [M, 3 kp] bf16, then (at
+    // xs32_off) the fp32 shifted x of the non-finite fallback, the fallback flag (at
+    // flag_off), with more than one range the fp32 partial sums [M, part_pitch] (at
+    // part_off), then the split W_enc of one range [3 kp, w_pitch] bf16.
     bool emulate;
-    int64_t kp, xs32_pitch;
-    size_t xs32_off, flag_off;
+    int nkc;
+    int64_t kc, kp, xs32_pitch, part_pitch;
+    size_t xs32_off, flag_off, part_off;
 };
 
 int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int variant, EncodePlan *pl) {
@@ -273,11 +276,9 @@ int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int vari
     pl->emulate = false;
     if (wdt == SF_F32) {
         // IEEE products (fp32 x, TF32 not allowed) run split-precision on the bf16 tensor
-        // cores when asked for (a tcgen05 variant) or, under AUTO, up to kEmuMaxAutoK;
-        // otherwise on the CUDA-core kernel. TF32 products on the tensor cores.
+        // cores unless the CUDA-core kernel is asked for; TF32 products on the tensor cores.
         const bool ieee = !allow_tf32 && x->dtype == SF_F32;
         tc = variant != SF_VARIANT_SIMT;
-        if (ieee && variant == SF_VARIANT_AUTO && K > kEmuMaxAutoK) tc = false;
         pl->emulate = ieee && tc;
     } else {
         tc = true;
@@ -306,12 +307,18 @@ int plan_encode(const sf_matrix *x, const sf_matrix *W, int allow_tf32, int vari
     if (pl->emulate) {
         pl->ab_fmt = 1;
         pl->mma_dtype = SF_BF16;
-        pl->kp = round_up(K > 0 ? K : 1, kEmuKBlock);
+        const int64_t k1 = K > 0 ? K : 1;
+        const int64_t ranges = (k1 + kEmuMaxRangeK - 1) / kEmuMaxRangeK;
+        pl->kc = ranges == 1 ? k1 : round_up((k1 + ranges - 1) / ranges, kEmuKBlock);
+        pl->nkc = (int)((k1 + pl->kc - 1) / pl->kc);
+        pl->kp = round_up(pl->kc, kEmuKBlock);
         pl->a_pitch = 3 * pl->kp;
-        pl->xs32_pitch = round_up(K > 0 ? K : 1, 8);
+        pl->xs32_pitch = round_up(k1, 8);
         pl->xs32_off = (size_t)round_up(M * pl->a_pitch * 2, 256);
         pl->flag_off = pl->xs32_off + (size_t)round_up(M * pl->xs32_pitch * 4, 256);
-        pl->xs_bytes = pl->flag_off + 256;
+        pl->part_off = pl->flag_off + 256;
+        pl->part_pitch = round_up(N > 0 ? N : 1, kCsrTile);  // whole 256-column tiles
+        pl->xs_bytes = pl->part_off + (pl->nkc > 1 ? (size_t)round_up(M * pl->part_pitch * 4, 256) : 0);
         pl->w_direct = false;
         pl->b_mn = true;
         pl->w_pitch = round_up(N > 0 ? N : 1, 8);
@@ -424,24 +431,27 @@ int run_repack(const sf_matrix *W, void *wp, int64_t pitch, bool mn_major, cudaS
 // operand split (split-precision fp32), or the shifted copy of x and, when TMA cannot read
 // W_enc in place, its repacked copy.
 int prepare_tc(const EncodePlan &pl, const sf_matrix *x, const sf_matrix *W, const sf_vector *b_dec, uint8_t *ws,
-               cudaStream_t s, GemmOperands &g) {
+               cudaStream_t s, GemmOperands &g, int range = 0) {
     g = GemmOperands{};
     g.M = x->rows;
     g.N = W->cols;
     void *wp = ws + round_up((int64_t)pl.xs_bytes, 256);
     if (pl.emulate) {
+        // K range `range`: columns [k0, k0 + kc) of x and rows of W_enc
+        const int64_t k0 = range * pl.kc;
+        const int64_t kr = std::min<int64_t>(pl.kc, x->cols - k0);
         EmuOperands e{};
-        e.x = static_cast<const float *>(x->data);
+        e.x = static_cast<const float *>(x->data) + k0 * x->stride_col;
         e.M = x->rows;
-        e.K = x->cols;
+        e.K = kr;
         e.sxm = x->stride_row;
         e.sxk = x->stride_col;
         if (b_dec && b_dec->data) {
-            e.b_dec = b_dec->data;
+            e.b_dec = static_cast<const uint8_t *>(b_dec->data) + k0 * b_dec->stride * (int64_t)dtype_size(b_dec->dtype);
             e.b_dtype = b_dec->dtype;
             e.b_stride = b_dec->stride;
         }
-        e.W = static_cast<const float *>(W->data);
+        e.W = static_cast<const float *>(W->data) + k0 * W->stride_row;
         e.N = W->cols;
         e.swk = W->stride_row;
         e.swn = W->stride_col;
@@ -450,6 +460,7 @@ int prepare_tc(const EncodePlan &pl, const sf_matrix *x, const sf_matrix *W, con
         e.kp = pl.kp;
         e.b_pitch = pl.w_pitch;
         e.flag = reinterpret_cast<unsigned *>(ws + pl.flag_off);
+        e.reset_flag = range == 0;
         const int st = emu_split_operands(e, s);
         if (st) return st;
         g.a = ws;
@@ -482,6 +493,37 @@ int prepare_tc(const EncodePlan &pl, const sf_matrix *x, const sf_matrix *W, con
     if (st) return st;
     g.b = wp;
     g.b_pitch = pl.w_pitch;
+    return SF_OK;
+}
+
+// The split-precision encode over its K ranges: ranges before the last store (the first) or
+// add to (the others) the fp32 partial sums with the raw epilogue; the last runs `final`
+// (the dense or CSR epilogue) with those partial sums added to its accumulators.
+template <typename Final>
+int run_emulated(const EncodePlan &pl, const sf_matrix *x, const sf_matrix *W, const sf_vector *b_dec,
+                 const sf_vector *b_enc, uint8_t *ws, int variant, cudaStream_t s, Final final) {
+    float *part = reinterpret_cast<float *>(ws + pl.part_off);
+    for (int r = 0; r < pl.nkc; ++r) {
+        GemmOperands g;
+        int st = prepare_tc(pl, x, W, b_dec, ws, s, g, r);
+        if (st) return st;
+        if (r + 1 == pl.nkc) return final(g, pl.nkc > 1 ? part : nullptr, pl.part_pitch);
+        EpilogueArgs raw{};
+        raw.b_enc = b_enc->data;  // staged by the epilogue, unused by a raw pass
+        raw.b_enc_dtype = b_enc->dtype;
+        raw.b_enc_stride = b_enc->stride;
+        raw.activation = SF_ACT_RELU;
+        raw.out = part;
+        raw.out_dtype = SF_F32;
+        raw.out_sm = pl.part_pitch;
+        raw.out_sn = 1;
+        raw.out_vec = 1;
+        raw.raw = 1;
+        raw.c_in = r > 0 ? part : nullptr;
+        raw.c_in_pitch = pl.part_pitch;
+        st = encode_tc_dense(g, raw, variant, s);
+        if (st) return st;
+    }
     return SF_OK;
 }
 
@@ -602,11 +644,21 @@ int sf_fused_encode(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector 
                                static_cast<const float *>(W_enc->data), W_enc->stride_row, W_enc->stride_col, M, N,
                                K, ep, s);
     }
+    if (pl.emulate) {
+        st = run_emulated(pl, x, W_enc, b_dec, b_enc, ws, variant, s,
+                          [&](const GemmOperands &g, const float *part, int64_t pitch) {
+                              EpilogueArgs e = ep;
+                              e.c_in = part;
+                              e.c_in_pitch = pitch;
+                              return encode_tc_dense(g, e, variant, s);
+                          });
+        if (st) return st;
+        return run_emu_fallback(pl, x, W_enc, b_dec, ws, ep, nullptr, s);
+    }
     GemmOperands g;
     st = prepare_tc(pl, x, W_enc, b_dec, ws, s, g);
-    if (!st) st = encode_tc_dense(g, ep, variant, s);
-    if (st || !pl.emulate) return st;
-    return run_emu_fallback(pl, x, W_enc, b_dec, ws, ep, nullptr, s);
+    if (st) return st;
+    return encode_tc_dense(g, ep, variant, s);
 }
 
 int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vector *b_enc, const sf_vector *b_dec,
@@ -663,11 +715,21 @@ int sf_encode_csr_stage(const sf_matrix *x, const sf_matrix *W_enc, const sf_vec
                                static_cast<const float *>(W_enc->data), W_enc->stride_row, W_enc->stride_col, M, N,
                                K, ep, s, &csr);
     }
+    if (pl.emulate) {
+        st = run_emulated(pl, x, W_enc, b_dec, b_enc, ws, SF_VARIANT_AUTO, s,
+                          [&](const GemmOperands &g, const float *part, int64_t pitch) {
+                              EpilogueArgs e = ep;
+                              e.c_in = part;
+                              e.c_in_pitch = pitch;
+                              return encode_tc_csr(g, e, csr, s);
+                          });
+        if (st) return st;
+        return run_emu_fallback(pl, x, W_enc, b_dec, ws, ep, &csr, s);
+    }
     GemmOperands g;
     st = prepare_tc(pl, x, W_enc, b_dec, ws, s, g);
-    if (!st) st = encode_tc_csr(g, ep, csr, s);
-    if (st || !pl.emulate) return st;
-    return run_emu_fallback(pl, x, W_enc, b_dec, ws, ep, &csr, s);
+    if (st) return st;
+    return encode_tc_csr(g, ep, csr, s);
 }
 
 int sf_csr_place(const int32_t *tile_counts, const int32_t *tile_offsets, int64_t M, int64_t d_sae,

@@ -17,9 +17,10 @@
 // that already holds the small ones (issuing them largest first measured ~7x the error).
 //
 // Layout: a = [x0 | x1 | x2] as one [M, 3 kp] bf16 matrix and b = [W0 ; W1 ; W2] as one
-// [3 kp, N] N-contiguous bf16 matrix, kp = d_in rounded up to the GEMM's 64-element K block
-// with zero padding, so every K block lies inside one segment. The GEMM's TMA producer maps
-// its 6 kp/64 K blocks onto (a segment, b segment) pairs: nothing is stored twice.
+// [3 kp, N] N-contiguous bf16 matrix, kp = the K range rounded up to the GEMM's 64-element
+// K block with zero padding, so every K block lies inside one segment. The GEMM's TMA
+// producer maps its 6 kp/64 K blocks onto (a segment, b segment) pairs: nothing is stored
+// twice. A d_in above kEmuMaxRangeK is split into K ranges, one split and one GEMM each.
 //
 // Non-finite operands: an inf or NaN in x - b_dec or in W_enc would meet the zero parts of
 // the other operand (inf * 0 = NaN where IEEE gives inf * w = inf). The split kernels raise a
@@ -181,7 +182,8 @@ bool aligned16_ptr(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u
 }  // namespace
 
 int emu_split_operands(const EmuOperands &e, cudaStream_t s) {
-    int st = check_cuda(cudaMemsetAsync(e.flag, 0, sizeof(unsigned), s), "emulated encode flag reset");
+    int st = SF_OK;
+    if (e.reset_flag) st = check_cuda(cudaMemsetAsync(e.flag, 0, sizeof(unsigned), s), "emulated encode flag reset");
     if (st) return st;
     if (e.M > 0) {
         const bool xvec = e.sxk == 1 && (e.sxm % 4) == 0 && aligned16_ptr(e.x);

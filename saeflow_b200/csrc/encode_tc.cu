@@ -106,7 +106,40 @@ struct TcParams {
     int seg_kb;
     uint32_t seg_a, seg_b;
     const unsigned *skip;
+    // K-range partial sums (see EpilogueArgs): c_in added to the accumulators; raw: store them
+    const float *c_in;
+    int64_t c_in_pitch;
+    int raw;
 };
+
+// TMEM accumulators of 32 columns at (row, col0) plus the partial sum of the earlier K ranges
+// (fp32, round to nearest); the partial buffer is padded to whole tiles, so every column of
+// a tile is in bounds.
+#ifndef SF_NO_PARTIAL
+#define SF_NO_PARTIAL 0
+#endif
+__device__ __forceinline__ void add_partial(const TcParams &p, int row, int col0, uint32_t (&r)[32]) {
+    if (SF_NO_PARTIAL || p.c_in == nullptr || row >= p.M) return;
+    // plain loads: a raw pass reads and then rewrites these same addresses
+    const float4 *src = reinterpret_cast<const float4 *>(p.c_in + (int64_t)row * p.c_in_pitch + col0);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 v = src[j / 4];
+        r[j + 0] = __float_as_uint(__uint_as_float(r[j + 0]) + v.x);
+        r[j + 1] = __float_as_uint(__uint_as_float(r[j + 1]) + v.y);
+        r[j + 2] = __float_as_uint(__uint_as_float(r[j + 2]) + v.z);
+        r[j + 3] = __float_as_uint(__uint_as_float(r[j + 3]) + v.w);
+    }
+}
+
+// Raw epilogue of one 32-column chunk: the fp32 sums themselves (no bias, no activation) to
+// the partial buffer, whole chunks (the buffer is padded to whole tiles).
+__device__ __forceinline__ void raw_chunk(const TcParams &p, const uint32_t (&r)[32], int row, int col0) {
+    if (row >= p.M) return;
+    uint4 *dst = reinterpret_cast<uint4 *>(reinterpret_cast<float *>(p.out) + (int64_t)row * p.out_sm + col0);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) dst[j / 4] = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+}
 
 // TMA K coordinates of K block kb in A and in B. Plain GEMM: both kb * bk. Split-operand
 // schedule: block kb lies in segment pair s = kb / seg_kb, whose A and B segments come from
@@ -471,14 +504,17 @@ __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, 
     uint32_t masks[NC];
     int cnt = 0;
     uint32_t ra[32], rb[32];
+    const int col_base = n_blk * kBN;
     tmem_ld_32x32b_x32(taddr, ra);
     tmem_ld_wait();
 #pragma unroll
     for (int c = 0; c < NC; c += 2) {
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
+        add_partial(p, row, col_base + c * 32, ra);
         masks[c] = csr_chunk_mask(&sh->bias[buf][c * 32], &sh->thr[buf][c * 32], ra);
         tmem_ld_wait();
         if (c + 2 < NC) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
+        add_partial(p, row, col_base + (c + 1) * 32, rb);
         masks[c + 1] = csr_chunk_mask(&sh->bias[buf][(c + 1) * 32], &sh->thr[buf][(c + 1) * 32], rb);
         if (c + 2 < NC) tmem_ld_wait();
     }
@@ -515,7 +551,10 @@ __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, 
                 uint32_t rr[32];
                 tmem_ld_32x32b_x32(taddr + c * 32, rr);
                 tmem_ld_wait();
-                if (masks[c]) csr_chunk_emit<OT>(p, &sh->bias[buf][c * 32], rr, n_blk * kBN + c * 32, masks[c], o);
+                if (masks[c]) {
+                    add_partial(p, row, col_base + c * 32, rr);
+                    csr_chunk_emit<OT>(p, &sh->bias[buf][c * 32], rr, n_blk * kBN + c * 32, masks[c], o);
+                }
             }
         }
     }
@@ -533,11 +572,14 @@ __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShare
     constexpr int NC = kBN / 32;
     const bool full_tile = (n_blk + 1) * kBN <= p.N;
     int cnt = 0;
-    auto process = [&](const uint32_t(&r)[32], int c) {
+    auto process = [&](uint32_t(&r)[32], int c) {
         const int col0 = n_blk * kBN + c * 32;
         const float *bias = &sh->bias[buf][c * 32];
         if constexpr (MODE == kDense) {
-            if (full_tile)
+            add_partial(p, row, col0, r);
+            if (!SF_NO_PARTIAL && p.raw)
+                raw_chunk(p, r, row, col0);
+            else if (full_tile)
                 dense_chunk<OT, JUMP, true>(p, bias, &sh->thr[buf][c * 32], r, row, col0, pol_out, cnt);
             else
                 dense_chunk<OT, JUMP, false>(p, bias, &sh->thr[buf][c * 32], r, row, col0, pol_out, cnt);
@@ -1370,6 +1412,9 @@ int encode_tc_dense(const GemmOperands &g, const EpilogueArgs &ep, int variant, 
     p.out_sn = ep.out_sn;
     p.out_vec = ep.out_vec;
     p.row_nnz = ep.row_nnz;
+    p.c_in = ep.c_in;
+    p.c_in_pitch = ep.c_in_pitch;
+    p.raw = ep.raw;
     if (pair) return dispatch<kDense, 6, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
     return dispatch<kDense, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
 }
@@ -1402,6 +1447,8 @@ int encode_tc_csr(const GemmOperands &g, const EpilogueArgs &ep, const CsrArgs &
     p.stage_val = csr.stage_val;
     p.csr_state = csr.state;
     p.stage_cap = csr.cap;
+    p.c_in = ep.c_in;
+    p.c_in_pitch = ep.c_in_pitch;
     if (pair) return dispatch<kCsr, 6, true>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
     return dispatch<kCsr, 4, false>(g.ab_fmt, g.b_mn_major, tmA, tmB, p, 0, stream);
 }

@@ -55,6 +55,7 @@ struct EmuOperands {
     __nv_bfloat16 *b;
     int64_t kp, b_pitch;
     unsigned *flag;
+    bool reset_flag;  // zero *flag first (the first K range of a call)
 };
 constexpr int kEmuKBlock = 64;  // bf16 elements per GEMM K block: the segment padding
 constexpr int kEmuPairs = 6;
@@ -62,14 +63,16 @@ constexpr int kEmuPairs = 6;
 constexpr uint32_t kEmuSegA = 0x001012u;  // nibble s = A segment of pair s
 constexpr uint32_t kEmuSegB = 0x010210u;  // nibble s = B segment of pair s
 int emu_split_operands(const EmuOperands &e, cudaStream_t s);
-// Largest d_in the AUTO variant sends to the split-precision route. Its partial products are
-// exact, but the tensor cores round the running fp32 sum once per 16-product MMA, toward
-// zero, so the error of the large (x0, W0) term grows with d_in / 16 (a bias, not a random
-// walk): measured on B200 against float64, max |error| 7.8e-6 at d_in 768 (the CUDA-core
-// IEEE kernel: 7.1e-6), within the fp32 contract (rtol 1e-5, atol 1e-5) at 2304, 89 of
-// 51200 features outside it at 4096 (worst 1.6e-5). Up to 1024 the bound d_in/16 * 2^-24
-// (3.8e-6 relative) leaves a 2.6x margin; beyond, AUTO runs the CUDA-core kernel.
-constexpr int64_t kEmuMaxAutoK = 1024;
+// Largest K range one split-precision GEMM accumulates. Its partial products are exact, but
+// the tensor cores round the running fp32 sum once per 16-product MMA, toward zero, so the
+// error of the large (x0, W0) term grows with the range / 16 (a bias, not a random walk):
+// measured on B200 against float64, max |error| 7.8e-6 at d_in 768 (the CUDA-core IEEE
+// kernel: 7.1e-6), within the fp32 contract (rtol 1e-5, atol 1e-5) at 2304, 89 of 51200
+// features outside it at 4096 in one range (worst 1.6e-5). Up to 1024 the bound
+// range/16 * 2^-24 (3.8e-6 relative) leaves a 2.6x margin, so a larger d_in runs as K ranges
+// of at most this size, each accumulated from zero and added to the partial sum of the
+// earlier ranges in fp32 round-to-nearest (EpilogueArgs::c_in).
+constexpr int64_t kEmuMaxRangeK = 1024;
 
 // 1: the CTA-pair kernel for 16-bit operands builds its A tiles with converter warps that
 // read x itself and subtract b_dec on the way (no shifted copy of x in HBM, no shift pass).
@@ -96,6 +99,13 @@ struct EpilogueArgs {
     int64_t out_sm, out_sn;
     int out_vec;
     int32_t *row_nnz;
+    // K-range partial sums of the split-precision route (tensor-core kernels): c_in (fp32,
+    // row pitch c_in_pitch, padded to whole 256-column tiles) is added to the accumulators
+    // before anything else; raw (dense kernel only) stores the sums themselves to `out` (the
+    // same padded fp32 layout) with no bias, activation or count. c_in may equal out.
+    const float *c_in;
+    int64_t c_in_pitch;
+    int raw;
 };
 
 struct TopkArgs {

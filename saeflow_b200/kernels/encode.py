@@ -48,24 +48,20 @@ def _variant(config) -> int:
     return _VARIANTS[v]
 
 
-SPLIT_PRECISION_MAX_D_IN = 1024  # kEmuMaxAutoK of the library: the "auto" limit of the split route
+SPLIT_PRECISION_RANGE = 1024  # kEmuMaxRangeK of the library: d_in per split-precision K range
 
 
 def _uses_tensor_cores(x, W_enc, allow_tf32, variant) -> bool:
-    """Every kernel choice but "simt" runs on the tensor cores, except IEEE fp32 under "auto"
-    above SPLIT_PRECISION_MAX_D_IN, whose split-precision error would outgrow the fp32
-    tolerance (see _split_precision)."""
-    if variant == _abi.SF_VARIANT_SIMT:
-        return False
-    if variant == _abi.SF_VARIANT_AUTO and _split_precision(x, W_enc, allow_tf32):
-        return x.shape[1] <= SPLIT_PRECISION_MAX_D_IN
-    return True
+    """Every kernel choice but "simt" runs on the tensor cores (IEEE fp32 products there
+    are split-precision, see _split_precision)."""
+    return variant != _abi.SF_VARIANT_SIMT
 
 
 def _split_precision(x, W_enc, allow_tf32) -> bool:
     """fp32 x and W_enc with TF32 not allowed: the reference's IEEE products
     (encode.py:118-120), computed on the bf16 tensor cores from three-part splits of both
-    operands, smallest partial products first, to fp32-class accuracy."""
+    operands, smallest partial products first, to fp32-class accuracy; a d_in above
+    SPLIT_PRECISION_RANGE runs as K ranges whose sums are added in fp32."""
     return W_enc.dtype == torch.float32 and x.dtype == torch.float32 and not allow_tf32
 
 

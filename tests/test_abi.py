@@ -74,6 +74,11 @@ def test_workspace_sizes():
     assert need.value == 4096 * 3 * 768 * 2 + 4096 * 768 * 4 + 256 + 3 * 768 * 16384 * 2
     assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 2, ctypes.byref(need)) == 0
     assert need.value == 4096 * 768 * 4
+    # d_in 2304: three K ranges of 768, plus the fp32 partial sums [M, d_sae rounded up to 256]
+    x = _abi.SfMatrix(16, 0, 0, 4096, 2304, 2304, 1)
+    W = _abi.SfMatrix(16, 0, 0, 2304, 16384, 16384, 1)
+    assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0
+    assert need.value == 4096 * 3 * 768 * 2 + 4096 * 2304 * 4 + 256 + 4096 * 16384 * 4 + 3 * 768 * 16384 * 2
     x = _abi.SfMatrix(16, 0, 0, 10, 100, 100, 1)  # d_in 100 -> kp 128; d_sae 129 -> pitch 136
     W = _abi.SfMatrix(16, 0, 0, 100, 129, 129, 1)
     assert lib.sf_fused_encode_workspace(ctypes.byref(x), ctypes.byref(W), 0, 0, ctypes.byref(need)) == 0

@@ -101,17 +101,45 @@ def test_split_precision_strided_x_and_b_dec(x_layout):
     contract.assert_values_close(got.cpu()[~near], want[~near], torch.float32, what=x_layout)
 
 
-@pytest.mark.parametrize("d_in", [1025, 4096])
-def test_auto_keeps_wide_ieee_fp32_on_the_cuda_cores(d_in):
-    """Above d_in 1024 the tensor cores' per-MMA rounding of the running sum would outgrow
-    the fp32 tolerance (measured at d_in 4096: 89 of 51200 features outside it), so "auto"
-    runs the CUDA-core IEEE kernel there, within the contract."""
-    x, W, b_enc, b_dec = _operands(100, d_in, 512, seed=d_in)
-    got = fused_encode(x, W, b_enc, b_dec)
-    assert best_config()["variant"] == "simt"
+@pytest.mark.parametrize("d_in", [1025, 2304, 4096])
+def test_split_precision_k_ranges(d_in):
+    """Above d_in 1024 the tensor cores' per-MMA rounding of one running sum would outgrow
+    the fp32 tolerance (measured at d_in 4096 in one range: 89 of 51200 features outside
+    it), so the route runs K ranges of at most 1024, each accumulated from zero, and adds
+    their sums in fp32: within the contract, the error of the order of the CUDA-core IEEE
+    kernel's, and the encode straight to CSR identical to the dense route."""
+    x, W, b_enc, b_dec = _operands(300, d_in, 1500, seed=d_in)
+    rn = torch.zeros(300, dtype=torch.int32, device="cuda")
+    got = fused_encode(x, W, b_enc, b_dec, row_nnz=rn)
+    assert best_config()["variant"] == "tcgen05" and "split" in best_config()["operands"]
     want, _, pre = oracle.fused_encode(x.cpu(), W.cpu(), b_enc.cpu(), b_dec.cpu())
     near = contract.near_cut(pre)
     contract.assert_values_close(got.cpu()[~near], want[~near], torch.float32, what=f"d_in {d_in}")
+    simt = fused_encode(x, W, b_enc, b_dec, config={"variant": "simt"})
+    pre64 = _pre64(x, W, b_enc, b_dec)
+    mx, rms = _errors(got, pre64)
+    mx_s, rms_s = _errors(simt, pre64)
+    assert mx <= 4 * mx_s + 1e-7 and rms <= 3 * rms_s + 1e-8, (mx, rms, mx_s, rms_s)
+    csr = encode_csr(x, W, b_enc, b_dec)
+    ref = dense_to_csr(got, rn)
+    for a, b in zip(csr, ref):
+        assert torch.equal(a.view(torch.int32) if a.is_floating_point() else a,
+                           b.view(torch.int32) if b.is_floating_point() else b)
+    single = fused_encode(x, W, b_enc, b_dec, config={"variant": "tcgen05_1cta"})
+    contract.assert_values_close(single.cpu()[~near], want[~near], torch.float32, what="single-CTA ranges")
+
+
+def test_split_precision_nonfinite_in_a_later_k_range():
+    """An inf in the last K range's operands: the earlier ranges' partial sums are written,
+    the last range's GEMM exits, and the CUDA-core kernel computes the call (identical)."""
+    x, W, b_enc, b_dec = _operands(200, 2304, 700, seed=8)
+    x[5, 2200] = float("inf")
+    rn = torch.zeros(200, dtype=torch.int32, device="cuda")
+    got = fused_encode(x, W, b_enc, b_dec, row_nnz=rn)
+    rn_s = torch.zeros(200, dtype=torch.int32, device="cuda")
+    want = fused_encode(x, W, b_enc, b_dec, row_nnz=rn_s, config={"variant": "simt"})
+    assert not torch.isfinite(want).all()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32)) and torch.equal(rn, rn_s)
 
 
 @pytest.mark.parametrize("variant", ["tcgen05", "tcgen05_1cta"])
