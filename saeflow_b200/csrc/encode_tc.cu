@@ -115,11 +115,12 @@ struct TcParams {
 // TMEM accumulators of 32 columns at (row, col0) plus the partial sum of the earlier K ranges
 // (fp32, round to nearest); the partial buffer is padded to whole tiles, so every column of
 // a tile is in bounds.
-#ifndef SF_NO_PARTIAL
-#define SF_NO_PARTIAL 0
-#endif
+// PART: instantiated only for the split-precision route (a runtime test in every epilogue
+// cost the 16-bit kernels ~5% at config 2 through register pressure).
+template <bool PART>
 __device__ __forceinline__ void add_partial(const TcParams &p, int row, int col0, uint32_t (&r)[32]) {
-    if (SF_NO_PARTIAL || p.c_in == nullptr || row >= p.M) return;
+    if constexpr (!PART) return;
+    if (p.c_in == nullptr || row >= p.M) return;
     // plain loads: a raw pass reads and then rewrites these same addresses
     const float4 *src = reinterpret_cast<const float4 *>(p.c_in + (int64_t)row * p.c_in_pitch + col0);
 #pragma unroll
@@ -496,7 +497,7 @@ __device__ __forceinline__ void csr_chunk_emit(const TcParams &p, const float *b
 // CSR epilogue of one tile: pass 1 over all chunks finds each row's nonzeros, one atomicAdd
 // per warp reserves staging space for the warp's 32 rows, pass 2 re-reads from TMEM only the
 // chunks where some row of the warp has a nonzero and emits them.
-template <typename OT, typename Release>
+template <typename OT, bool PART, typename Release>
 __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, int row, int n_blk, int buf,
                                          uint32_t taddr, Release release) {
     constexpr int NC = kBN / 32;
@@ -510,11 +511,11 @@ __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, 
 #pragma unroll
     for (int c = 0; c < NC; c += 2) {
         tmem_ld_32x32b_x32(taddr + (c + 1) * 32, rb);
-        add_partial(p, row, col_base + c * 32, ra);
+        add_partial<PART>(p, row, col_base + c * 32, ra);
         masks[c] = csr_chunk_mask(&sh->bias[buf][c * 32], &sh->thr[buf][c * 32], ra);
         tmem_ld_wait();
         if (c + 2 < NC) tmem_ld_32x32b_x32(taddr + (c + 2) * 32, ra);
-        add_partial(p, row, col_base + (c + 1) * 32, rb);
+        add_partial<PART>(p, row, col_base + (c + 1) * 32, rb);
         masks[c + 1] = csr_chunk_mask(&sh->bias[buf][(c + 1) * 32], &sh->thr[buf][(c + 1) * 32], rb);
         if (c + 2 < NC) tmem_ld_wait();
     }
@@ -552,7 +553,7 @@ __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, 
                 tmem_ld_32x32b_x32(taddr + c * 32, rr);
                 tmem_ld_wait();
                 if (masks[c]) {
-                    add_partial(p, row, col_base + c * 32, rr);
+                    add_partial<PART>(p, row, col_base + c * 32, rr);
                     csr_chunk_emit<OT>(p, &sh->bias[buf][c * 32], rr, n_blk * kBN + c * 32, masks[c], o);
                 }
             }
@@ -564,7 +565,7 @@ __device__ __forceinline__ void csr_tile(const TcParams &p, const TcShared *sh, 
 // One tile of epilogue for this thread's row: reads the 256 fp32 accumulators of its TMEM
 // lane 32 columns at a time, loading chunk c+1 while chunk c is processed; `release` runs
 // once all TMEM reads of the tile are complete, so the MMA warp may reuse the buffer.
-template <int MODE, typename OT, bool JUMP, typename Release>
+template <int MODE, typename OT, bool JUMP, bool PART, typename Release>
 __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
                                                 int et, int row, int n_blk, int buf, uint32_t taddr,
                                                 uint64_t pol_out, TopkState &ts,
@@ -576,8 +577,8 @@ __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShare
         const int col0 = n_blk * kBN + c * 32;
         const float *bias = &sh->bias[buf][c * 32];
         if constexpr (MODE == kDense) {
-            add_partial(p, row, col0, r);
-            if (!SF_NO_PARTIAL && p.raw)
+            add_partial<PART>(p, row, col0, r);
+            if (PART && p.raw)
                 raw_chunk(p, r, row, col0);
             else if (full_tile)
                 dense_chunk<OT, JUMP, true>(p, bias, &sh->thr[buf][c * 32], r, row, col0, pol_out, cnt);
@@ -606,41 +607,41 @@ __device__ __forceinline__ void epilogue_tile_t(const TcParams &p, const TcShare
     if (MODE == kDense && p.row_nnz != nullptr && row < p.M && cnt != 0) atomicAdd(p.row_nnz + row, cnt);
 }
 
-template <int MODE, typename Release>
+template <int MODE, bool PART, typename Release>
 __device__ __forceinline__ void epilogue_tile(const TcParams &p, const TcShared *sh, unsigned long long *topk_lists,
                                               int et, int row, int n_blk, int buf, uint32_t taddr, uint64_t pol_out,
                                               TopkState &ts, Release release) {
     if constexpr (MODE == kCsr) {
         if (p.out_dtype == SF_BF16)
-            csr_tile<__nv_bfloat16>(p, sh, row, n_blk, buf, taddr, release);
+            csr_tile<__nv_bfloat16, PART>(p, sh, row, n_blk, buf, taddr, release);
         else if (p.out_dtype == SF_F16)
-            csr_tile<__half>(p, sh, row, n_blk, buf, taddr, release);
+            csr_tile<__half, PART>(p, sh, row, n_blk, buf, taddr, release);
         else
-            csr_tile<float>(p, sh, row, n_blk, buf, taddr, release);
+            csr_tile<float, PART>(p, sh, row, n_blk, buf, taddr, release);
         return;
     }
     if constexpr (MODE == kTopk) {
-        epilogue_tile_t<kTopk, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
+        epilogue_tile_t<kTopk, float, false, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
         return;
     }
     const bool jump = p.activation == SF_ACT_JUMPRELU;
     if (p.out_dtype == SF_BF16) {
         if (jump)
-            epilogue_tile_t<kDense, __nv_bfloat16, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
+            epilogue_tile_t<kDense, __nv_bfloat16, true, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
                                                          ts, release);
         else
-            epilogue_tile_t<kDense, __nv_bfloat16, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
+            epilogue_tile_t<kDense, __nv_bfloat16, false, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out,
                                                           ts, release);
     } else if (p.out_dtype == SF_F16) {
         if (jump)
-            epilogue_tile_t<kDense, __half, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
+            epilogue_tile_t<kDense, __half, true, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
         else
-            epilogue_tile_t<kDense, __half, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
+            epilogue_tile_t<kDense, __half, false, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
     } else {
         if (jump)
-            epilogue_tile_t<kDense, float, true>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
+            epilogue_tile_t<kDense, float, true, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
         else
-            epilogue_tile_t<kDense, float, false>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
+            epilogue_tile_t<kDense, float, false, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, release);
     }
 }
 
@@ -709,7 +710,7 @@ __device__ __forceinline__ uint4 shift_chunk(uint4 v, const float2 (&nb)[4]) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+template <int AB_FMT, bool B_MN, int MODE, int STAGES, bool PART>
 __global__ void __launch_bounds__(kThreads, 1)
     encode_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const TcParams p) {
@@ -889,7 +890,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
                 const int acc_now = acc;
-                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, [&] {
+                epilogue_tile<MODE, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, [&] {
                     tc_fence_before();
                     mbar_arrive(&sh->tmem_empty[acc_now]);
                 });
@@ -917,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // -------------------------------------------------------------------------------------
 // CTA-pair kernel (cluster of 2, tcgen05 cta_group::2): 256 x 256 tile per pair.
-template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+template <int AB_FMT, bool B_MN, int MODE, int STAGES, bool PART>
 __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kConvThreads : kThreads, 1)
     encode_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const TcParams p) {
@@ -1204,7 +1205,7 @@ __global__ void __launch_bounds__((AB_FMT != 2 && kFusedShift) ? kThreads + kCon
                 tc_fence_after();
                 const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + acc * kAccCols;
                 const uint32_t empty_leader = map_to_rank(smem_u32(&sh->tmem_empty[acc]), 0);
-                epilogue_tile<MODE>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, [&] {
+                epilogue_tile<MODE, PART>(p, sh, topk_lists, et, row, n_blk, buf, taddr, pol_out, ts, [&] {
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive_remote(empty_leader);
@@ -1267,10 +1268,10 @@ int make_map_2d(CUtensorMap *map, const void *base, int ab_fmt, uint64_t inner, 
     return SF_OK;
 }
 
-template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+template <int AB_FMT, bool B_MN, int MODE, int STAGES, bool PART>
 int launch_single(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
                   cudaStream_t stream) {
-    auto kern = encode_tc_kernel<AB_FMT, B_MN, MODE, STAGES>;
+    auto kern = encode_tc_kernel<AB_FMT, B_MN, MODE, STAGES, PART>;
     const size_t smem = 1024 + (size_t)STAGES * kStageBytes + sizeof(TcShared) + extra_smem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return check_cuda(e, "cudaFuncSetAttribute(encode_tc)");
@@ -1279,10 +1280,10 @@ int launch_single(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams
     return check_cuda(cudaGetLastError(), "encode_tc launch");
 }
 
-template <int AB_FMT, bool B_MN, int MODE, int STAGES>
+template <int AB_FMT, bool B_MN, int MODE, int STAGES, bool PART>
 int launch_pair(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p, size_t extra_smem,
                 cudaStream_t stream) {
-    auto kern = encode_tc2_kernel<AB_FMT, B_MN, MODE, STAGES>;
+    auto kern = encode_tc2_kernel<AB_FMT, B_MN, MODE, STAGES, PART>;
     constexpr int threads = (AB_FMT != 2 && kFusedShift) ? kThreads + kConvThreads : kThreads;
     const size_t smem = 1024 + (size_t)STAGES * (kBM * 128 + (kBN / 2) * 128) + sizeof(TcShared) + extra_smem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1309,12 +1310,21 @@ int launch_pair(const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &
 template <int MODE, int STAGES, bool PAIR>
 int dispatch(int ab_fmt, bool b_mn, const CUtensorMap &tmA, const CUtensorMap &tmB, const TcParams &p,
              size_t extra_smem, cudaStream_t s) {
-#define SF_LAUNCH(F, MN) \
-    (PAIR ? launch_pair<F, MN, MODE, STAGES>(tmA, tmB, p, extra_smem, s) \
-          : launch_single<F, MN, MODE, STAGES>(tmA, tmB, p, extra_smem, s))
-    if (ab_fmt == 1) return b_mn ? SF_LAUNCH(1, true) : SF_LAUNCH(1, false);
-    if (ab_fmt == 0) return b_mn ? SF_LAUNCH(0, true) : SF_LAUNCH(0, false);
-    return b_mn ? SF_LAUNCH(2, true) : SF_LAUNCH(2, false);
+#define SF_LAUNCH(F, MN, PART) \
+    (PAIR ? launch_pair<F, MN, MODE, STAGES, PART>(tmA, tmB, p, extra_smem, s) \
+          : launch_single<F, MN, MODE, STAGES, PART>(tmA, tmB, p, extra_smem, s))
+    if (p.c_in != nullptr || p.raw) {
+        // K-range partial sums: the split-precision route only (bf16 operands, MN-major B)
+        if constexpr (MODE == kTopk) {
+            return set_error(SF_ERR_UNSUPPORTED, "partial sums are not supported by the top-k epilogue");
+        } else {
+            if (ab_fmt != 1 || !b_mn) return set_error(SF_ERR_UNSUPPORTED, "partial sums need split bf16 operands");
+            return SF_LAUNCH(1, true, true);
+        }
+    }
+    if (ab_fmt == 1) return b_mn ? SF_LAUNCH(1, true, false) : SF_LAUNCH(1, false, false);
+    if (ab_fmt == 0) return b_mn ? SF_LAUNCH(0, true, false) : SF_LAUNCH(0, false, false);
+    return b_mn ? SF_LAUNCH(2, true, false) : SF_LAUNCH(2, false, false);
 #undef SF_LAUNCH
 }
 
