@@ -389,6 +389,13 @@ __device__ __forceinline__ void chunk_to_f32(const uint4 &u, float (&x)[16 / siz
     }
 }
 
+// 1: the consumers update their row accumulators two at a time with the packed fp32 FMA of
+// sm_100 (__ffma2_rn); 0: one fmaf each. Same bits either way.
+#ifndef SF_GATHER_FMA2
+#define SF_GATHER_FMA2 1
+#endif
+constexpr bool kGatherFma2 = SF_GATHER_FMA2 != 0;
+
 // Consumer warps a launch may have: with 3 or 4 chunks per thread the register budget allows 8.
 __host__ __device__ constexpr int gather_max_warps(int cpt) { return cpt >= 3 ? 8 : kGatherMaxWarps; }
 
@@ -694,10 +701,26 @@ __global__ void __launch_bounds__(32 * (1 + gather_max_warps(CPT)), 1) csc_gathe
         for (int k = 0; k < CPT; ++k) {
             float x[EPV];
             chunk_to_f32<RT>(u[k], x);
+            if constexpr (kGatherFma2) {
+                // two accumulators per packed FMA (each lane bit-identical to fmaf); the dot
+                // product keeps its one scalar chain, so its summation order is unchanged
 #pragma unroll
-            for (int e = 0; e < EPV; ++e) {
-                acc[k][e] = fmaf(vf, x[e], acc[k][e]);
-                if constexpr (DOT) dp = fmaf(x[e], wv[k][e], dp);
+                for (int e = 0; e < EPV; e += 2) {
+                    const float2 r = __ffma2_rn(make_float2(vf, vf), make_float2(x[e], x[e + 1]),
+                                                make_float2(acc[k][e], acc[k][e + 1]));
+                    acc[k][e] = r.x;
+                    acc[k][e + 1] = r.y;
+                }
+                if constexpr (DOT) {
+#pragma unroll
+                    for (int e = 0; e < EPV; ++e) dp = fmaf(x[e], wv[k][e], dp);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPV; ++e) {
+                    acc[k][e] = fmaf(vf, x[e], acc[k][e]);
+                    if constexpr (DOT) dp = fmaf(x[e], wv[k][e], dp);
+                }
             }
         }
         if (sums) vsum += (double)vf;
