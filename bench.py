@@ -275,6 +275,15 @@ class ClockSampler:
                 "samples": len(self.samples), "samples_under_load": len(loaded), "source": "nvml 10 ms"}
 
 
+def ieee_launches(d_in):
+    """Kernels per forward chunk on the IEEE fp32 split route: per K range (at most 1024 of
+    d_in, ranges of a multiple of 64 as even as possible) the x split, the W_enc split and
+    the GEMM; then the two gated fallback launches, the indptr scan, placement and decode."""
+    ranges = -(-d_in // 1024)
+    kc = -(-(-(-d_in // ranges)) // 64) * 64 if ranges > 1 else d_in
+    return 3 * -(-d_in // kc) + 5
+
+
 def encode_errors(sae, x, f, rows=4096):
     """Max and rms |error| of encoder output rows f[:rows] against the float64 product of the
     same operands (activation applied to the float64 pre-activations)."""
@@ -398,7 +407,7 @@ def run_ours(args, rank, world, device):
             return out
         # shift, encode, indptr scan, compact, decode (IEEE fp32: two operand splits and two
         # gated fallback launches in place of the shift)
-        launches_per_step = 8 if cfg_id == 1 else 5
+        launches_per_step = ieee_launches(c["d_in"]) if cfg_id == 1 else 5
     else:
         # Encode straight to CSR (what saeflow_b200.encode_sparse runs): no dense features.
         if cfg_id != 5:
@@ -428,7 +437,7 @@ def run_ours(args, rank, world, device):
         # per chunk: shift, encode+stage, indptr scan, place, decode; IEEE fp32 (config 1): the
         # operand splits of x and W_enc, the encode, the two gated non-finite-fallback launches
         # (no-ops on finite inputs), indptr scan, place, decode
-        launches_per_step = (8 if cfg_id == 1 else 5) * quads
+        launches_per_step = (ieee_launches(c["d_in"]) if cfg_id == 1 else 5) * quads
 
     def barrier():
         if world > 1:
