@@ -414,10 +414,11 @@ def run_ours(args, rank, world, device):
             x = make_tokens(cfg_id, rank, device, T)
 
         # What saeflow_b200.forward runs: the CSR stays on the device (no host sync mid-step),
-        # batches above FORWARD_CHUNK_ROWS rows as consecutive chunks into one output.
-        from saeflow_b200.ops import FORWARD_CHUNK_ROWS
+        # batches above forward_launch_rows(sae) rows as consecutive chunks into one output.
+        from saeflow_b200.ops import forward_launch_rows
 
-        chunks = [(r0, min(T, r0 + FORWARD_CHUNK_ROWS)) for r0 in range(0, T, FORWARD_CHUNK_ROWS)]
+        R = forward_launch_rows(sae)
+        chunks = [(r0, min(T, r0 + R)) for r0 in range(0, T, R)]
         quads = len(chunks)
         out_buf = torch.empty(T, c["d_in"], dtype=c["dtype"], device=device)
 

@@ -65,11 +65,23 @@ def _forward_async(sae, x, out=None, *, add_b_dec=True, out_dtype=None):
     return sparse_decode(*csr, sae.W_dec, b_dec, out=out, out_dtype=out_dtype), overflow
 
 
-# Rows per encode launch of forward(): larger batches run as consecutive launches of this
-# size. It bounds the CSR staging (M x d_sae/256 tile counts) and, measured on B200 at
-# d_sae = 2^20, keeps the power-capped SM clock higher than one launch over every row
-# (1327 MHz at 16384 rows per launch against 960 MHz at 262144).
+# Rows per encode launch of forward(): larger batches run as consecutive launches. At most
+# FORWARD_CHUNK_ROWS, which bounds the CSR staging (M x d_sae/256 tile counts), and at most
+# FORWARD_LAUNCH_MACS multiply-adds of the encoder GEMM: long launches meet the 1000 W power
+# cap at a lower SM clock. Measured on B200 at config 5 (d_in 2304, d_sae 2^20, one GPU):
+# 16384-row launches (4e13 multiply-adds) ran at 1237-1320 MHz, 1418 ms per 262144 tokens;
+# 8192-row launches at 1455-1500 MHz, 1275 ms; 4096 and 2048 rows the same as 8192 (one
+# 262144-row launch: 960 MHz). Config 2 (16384 x 2304 x 65536 = 2.5e12) stays one launch.
 FORWARD_CHUNK_ROWS = 16384
+FORWARD_LAUNCH_MACS = 2e13
+
+
+def forward_launch_rows(sae):
+    """Rows per encode launch of forward() for this SAE: a multiple of 1024 (at least 1024)
+    up to FORWARD_CHUNK_ROWS, within FORWARD_LAUNCH_MACS multiply-adds."""
+    per_row = max(1, sae.W_enc.shape[0] * sae.W_enc.shape[1])
+    rows = int(FORWARD_LAUNCH_MACS // per_row) // 1024 * 1024
+    return max(1024, min(FORWARD_CHUNK_ROWS, rows))
 
 
 def forward(sae, x):
@@ -78,18 +90,19 @@ def forward(sae, x):
     The CSR stays on the device between the two, so nothing waits on the host between the
     encoder and the decoder; the one host read (as in the reference, decode.py:88) comes at
     the end and checks that the CSR staging did not overflow (a chunk that overflowed is
-    redone through encode_sparse's exact-size route). Batches above FORWARD_CHUNK_ROWS rows
-    run as consecutive chunks into one output."""
+    redone through encode_sparse's exact-size route). Batches above forward_launch_rows(sae)
+    rows run as consecutive chunks into one output."""
     M = x.shape[0]
-    if M <= FORWARD_CHUNK_ROWS:
+    R = forward_launch_rows(sae)
+    if M <= R:
         out, overflow = _forward_async(sae, x)
         if overflow is not None and int(overflow):
             out = decode_sparse(sae, encode_sparse(sae, x))
         return out
     out = torch.empty(M, sae.W_dec.shape[1], dtype=sae.W_dec.dtype, device=x.device)
     flags = []
-    for r0 in range(0, M, FORWARD_CHUNK_ROWS):
-        r1 = min(M, r0 + FORWARD_CHUNK_ROWS)
+    for r0 in range(0, M, R):
+        r1 = min(M, r0 + R)
         _, overflow = _forward_async(sae, x[r0:r1], out[r0:r1])
         if overflow is not None:
             flags.append((r0, r1, overflow))
@@ -200,7 +213,7 @@ def forward_host_async(sae, x, out=None, *, chunk_tokens=8192):
     and the last copy out exposed. x and out must stay untouched until wait() returns.
 
     chunk_tokens=None: no split for overlap inside the call (each chunk costs ~0.1 ms at
-    config 2), only forward()'s FORWARD_CHUNK_ROWS launches; the choice for a stream of
+    config 2), only forward()'s launches (forward_launch_rows); the choice for a stream of
     batches, whose copies overlap the neighbouring calls' compute instead."""
     if x.is_cuda:
         raise ValueError("forward_host takes a host tensor; call forward() for a device tensor")
@@ -225,7 +238,7 @@ def forward_host_async(sae, x, out=None, *, chunk_tokens=8192):
     compute = torch.cuda.current_stream(dev)
     h2d, d2h = _streams(dev)
     whole = M * (K * x.element_size() + D * out.element_size()) <= WHOLE_BATCH_DEVICE_BYTES
-    plan = _even_split(M, FORWARD_CHUNK_ROWS) if chunk_tokens is None else _chunk_plan(M, chunk_tokens)
+    plan = _even_split(M, forward_launch_rows(sae)) if chunk_tokens is None else _chunk_plan(M, chunk_tokens)
     rows = M if whole else max(plan)
     nbuf = 1 if whole else 2
     # Each device buffer comes from the pool of the stream that writes it (x: the copy-in

@@ -453,7 +453,7 @@ def test_forward_host_async_pipelined_calls(whole, monkeypatch):
         assert p.wait() is o
         assert torch.equal(o.view(torch.int16), w.view(torch.int16))
     assert pend[0].wait() is outs[0]  # a second wait returns the same output
-    # chunk_tokens=None: one launch per FORWARD_CHUNK_ROWS rows, as forward() on the device
+    # chunk_tokens=None: forward()'s launches (forward_launch_rows), as forward() on the device
     for x in xs:
         assert torch.equal(forward_host_async(sae, x, chunk_tokens=None).wait().view(torch.int16),
                            ops.forward(sae, x.cuda()).cpu().view(torch.int16))
